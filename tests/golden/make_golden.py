@@ -1,0 +1,257 @@
+"""Generate golden fixtures by running the reference Memintelli package on CPU.
+
+Run in a container where the reference source tree is available:
+
+    python tests/golden/make_golden.py --ref /root/reference [--seeds 256]
+
+It writes ``tests/golden/cases.npz`` (deterministic noise-free cases: inputs or
+their seed, the reference's packed slice codes, block maxima / exponents and
+fp32 outputs) and ``tests/golden/noise_stats.json`` (per-seed SNR and error
+moments of the reference's noisy path, for statistical parity).
+
+The reference imports matplotlib at module level; it is stubbed because only
+the arithmetic is exercised.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+import time
+import types
+
+import numpy as np
+import torch
+
+
+def _stub_matplotlib():
+    class _Stub(types.ModuleType):
+        def __getattr__(self, k):
+            if k.startswith("__"):
+                raise AttributeError(k)
+            return lambda *a, **kw: None
+
+    m = _Stub("matplotlib")
+    m.pyplot = _Stub("matplotlib.pyplot")
+    sys.modules.setdefault("matplotlib", m)
+    sys.modules.setdefault("matplotlib.pyplot", m.pyplot)
+
+
+NOISE_FREE = dict(write_variation=0.0, read_variation=0.0, vnoise=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0)
+
+# name -> case spec.  x/W come either from a torch seed (stored as "seed") or are stored.
+CASES = {
+    # example 1 shapes (config 0), noise-free engine, training path (_dot) as the example runs it
+    "cfg0_int": dict(xs=(400, 500), ws=(500, 600), seed=42, store_inputs=False, bw_e=None,
+                     sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                     eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=False),
+    "cfg0_fp": dict(xs=(400, 500), ws=(500, 600), seed=42, store_inputs=False, bw_e=8,
+                    sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                    eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=False),
+    "cfg0_int_stuck": dict(xs=(400, 500), ws=(500, 600), seed=42, store_inputs=False, bw_e=None,
+                           sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                           eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, rate_stuck_HGS=0.001),
+                           inference=True),
+    # tie-free settings: radc = D + 1 (lossless) and an odd-denominator lossy ADC
+    "tiefree_lossless": dict(xs=(96, 300), ws=(300, 160), seed=7, store_inputs=True, bw_e=None,
+                             sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                             eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=289), inference=True),
+    "tiefree_lossy": dict(xs=(96, 300), ws=(300, 160), seed=8, store_inputs=True, bw_e=8,
+                          sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                          eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=33), inference=True),
+    # batched (3-D) input, odd sizes
+    "batch3d": dict(xs=(2, 19, 70), ws=(70, 45), seed=1, store_inputs=True, bw_e=None,
+                    sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 64), wp=(32, 32), wq=(64, 64),
+                    eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=True),
+    "batch3d_train": dict(xs=(3, 33, 100), ws=(100, 70), seed=11, store_inputs=True, bw_e=8,
+                          sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 64), wp=(32, 32), wq=(64, 64),
+                          eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=False),
+    # block floating point with a non-dyadic ADC ratio (config 2's radc)
+    "bfp_radc1024": dict(xs=(37, 100), ws=(100, 45), seed=2, store_inputs=True, bw_e=8,
+                         sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 64), wp=(32, 32), wq=(64, 64),
+                         eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=1024), inference=True),
+    # 64-deep crossbar (config 3 style)
+    "p64": dict(xs=(50, 200), ws=(200, 130), seed=3, store_inputs=True, bw_e=None,
+                sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 64), xq=(1, 64), wp=(64, 64), wq=(64, 64),
+                eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=True),
+    # 2-D input tiles, 16 levels (memmat_tensor.py self-test style)
+    "xtile_g16": dict(xs=(70, 130), ws=(130, 90), seed=4, store_inputs=True, bw_e=None,
+                      sx=[1, 1, 2, 4], sw=[1, 1, 2, 4], xp=(64, 64), xq=(64, 64), wp=(64, 64), wq=(64, 64),
+                      eng=dict(HGS=1e-5, LGS=1e-7, rdac=16, g_level=16, radc=2 ** 16), inference=True),
+    # per-weight-slice ADC resolution list
+    "radc_list": dict(xs=(64, 150), ws=(150, 100), seed=5, store_inputs=True, bw_e=None,
+                      sx=[1, 1, 2, 2], sw=[1, 1, 2, 2], xp=(64, 64), xq=(64, 64), wp=(64, 64), wq=(64, 64),
+                      eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=[2 ** 12, 2 ** 11, 2 ** 10, 2 ** 9]),
+                      inference=True),
+    # per-column weight tiles, 2-slice (example 11 geometry)
+    "percol_2slice": dict(xs=(40, 150), ws=(150, 33), seed=6, store_inputs=True, bw_e=None,
+                          sx=[1, 1], sw=[1, 1], xp=(1, 64), xq=(1, 64), wp=(64, 1), wq=(64, 1),
+                          eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=True),
+    # string granularities
+    "gran_strings": dict(xs=(30, 90), ws=(90, 50), seed=9, store_inputs=True, bw_e=None,
+                         sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq="per-row", wp=(32, 32), wq="per-matrix",
+                         eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=True),
+    # both stuck-at kinds
+    "stuck_both": dict(xs=(48, 128), ws=(128, 200), seed=10, store_inputs=True, bw_e=None,
+                       sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                       eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, rate_stuck_HGS=0.02,
+                                rate_stuck_LGS=0.03), inference=True),
+    # write variation only (deterministic: fixed-seed draw), compared with a loose tolerance
+    "write_var": dict(xs=(64, 128), ws=(128, 64), seed=12, store_inputs=True, bw_e=None,
+                      sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32), wq=(128, 128),
+                      eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.05),
+                      inference=True),
+}
+
+
+def make_inputs(spec, name):
+    if spec["store_inputs"]:
+        g = torch.Generator().manual_seed(spec["seed"])
+        x = torch.randn(*spec["xs"], generator=g)
+        w = torch.randn(*spec["ws"], generator=g)
+        return x, w
+    torch.manual_seed(spec["seed"])
+    x = torch.randn(*spec["xs"])
+    w = torch.randn(*spec["ws"])
+    return x, w
+
+
+def add_zero_blocks(x, w, wq):
+    """Zero one input row and the first weight quant block (all-zero-block path)."""
+    x = x.clone()
+    w = w.clone()
+    x[..., 3, :] = 0.0
+    w[0:wq[0], 0:wq[1]] = 0.0
+    return x, w
+
+
+def run_case(name, spec, DPETensor, SlicedData):
+    eng_kw = dict(NOISE_FREE)
+    eng_kw.update(spec["eng"])
+    eng = DPETensor(device=torch.device("cpu"), **eng_kw)
+    x, w = make_inputs(spec, name)
+    if name in ("batch3d", "stuck_both"):
+        x, w = add_zero_blocks(x, w, spec["wq"])
+    xs = SlicedData(torch.tensor(spec["sx"]), bw_e=spec["bw_e"], is_weight=False, paral_size=spec["xp"],
+                    quant_gran=spec["xq"], device=torch.device("cpu"), inference=spec["inference"])
+    ws = SlicedData(torch.tensor(spec["sw"]), bw_e=spec["bw_e"], is_weight=True, paral_size=spec["wp"],
+                    quant_gran=spec["wq"], device=torch.device("cpu"), inference=spec["inference"])
+    # the reference needs sliced_data of the weight for G; inference=True frees it afterwards.
+    ws_keep = SlicedData(torch.tensor(spec["sw"]), bw_e=spec["bw_e"], is_weight=True, paral_size=spec["wp"],
+                         quant_gran=spec["wq"], device=torch.device("cpu"), inference=False)
+    ws_keep.slice_data_imp(eng, w)
+    ws.slice_data_imp(eng, w)
+    xs.slice_data_imp(eng, x)
+    y = eng(xs, ws)
+    out = {
+        "y": y.numpy().astype(np.float32),
+        "x_packed": pack_codes(xs.sliced_data, spec["sx"]),
+        "w_packed": pack_codes(ws_keep.sliced_data, spec["sw"]),
+        "x_max": xs.max_data.numpy().astype(np.float32),
+        "w_max": ws_keep.max_data.numpy().astype(np.float32),
+    }
+    if spec["bw_e"]:
+        out["x_ebias"] = xs.e_bias.numpy().astype(np.float32)
+        out["w_ebias"] = ws_keep.e_bias.numpy().astype(np.float32)
+    if not spec["inference"] and spec["store_inputs"]:
+        out["x_quantized"] = xs.quantized_data.numpy().astype(np.float32)
+    if spec["store_inputs"]:
+        out["x"] = x.numpy()
+        out["w"] = w.numpy()
+    else:
+        out["x_sum"] = np.array([float(x.double().sum()), float(w.double().sum())])
+    # fixed-seed fault fields (memmat_tensor.py:177-187) are regenerated by the tests from
+    # torch.Generator().manual_seed(123 / 42) over this G shape; store the shape and a checksum.
+    out["G_shape"] = np.array(ws_keep.G.shape)
+    if eng_kw.get("rate_stuck_HGS", 0) > 0 or eng_kw.get("rate_stuck_LGS", 0) > 0:
+        gen = torch.Generator().manual_seed(123)
+        out["stuck_field_sum"] = np.array([float(torch.rand(ws_keep.G.shape, generator=gen).double().sum())])
+    if eng_kw.get("write_variation", 0) > 0:
+        gen = torch.Generator().manual_seed(42)
+        wf = torch.normal(0, eng_kw["write_variation"], ws_keep.G.shape, generator=gen)
+        out["write_field_sum"] = np.array([float(wf.double().sum())])
+    return out
+
+
+def pack_codes(sliced, slice_method):
+    """Packed two's complement code per element from the reference slice planes (LSB-first)."""
+    sl = sliced.to(torch.int64)
+    widths = list(slice_method)[::-1]
+    packed = torch.zeros_like(sl.select(-3, 0))
+    off = 0
+    for t, wdt in enumerate(widths):
+        packed += sl.select(-3, t) << off
+        off += wdt
+    return packed.numpy().astype(np.uint8 if off <= 8 else np.int16)
+
+
+def noise_stats(n_seeds, DPETensor, SlicedData):
+    """Per-seed SNR and error moments of the reference's noisy path (config 0 engine)."""
+    res = {}
+    for bw_e in (None, 8):
+        key = "fp" if bw_e else "int"
+        rows = []
+        t0 = time.time()
+        for s in range(n_seeds):
+            g = torch.Generator().manual_seed(1000 + s)
+            x = torch.randn(400, 500, generator=g)
+            w = torch.randn(500, 600, generator=g)
+            ideal = (x.double() @ w.double()).numpy()
+            outs = []
+            for noisy in (True, False):
+                kw = dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.0,
+                          rate_stuck_HGS=0.001, rate_stuck_LGS=0.0,
+                          read_variation=0.05 if noisy else 0.0, vnoise=0.05 if noisy else 0.0)
+                torch.manual_seed(50_000 + s)
+                eng = DPETensor(device=torch.device("cpu"), **kw)
+                xs = SlicedData(torch.tensor([1, 1, 2, 2, 2]), bw_e=bw_e, is_weight=False, paral_size=(1, 32),
+                                quant_gran=(1, 128), device=torch.device("cpu"), inference=True)
+                ws = SlicedData(torch.tensor([1, 1, 2, 2, 2]), bw_e=bw_e, is_weight=True, paral_size=(32, 32),
+                                quant_gran=(128, 128), device=torch.device("cpu"), inference=True)
+                ws.slice_data_imp(eng, w)
+                xs.slice_data_imp(eng, x)
+                outs.append(eng(xs, ws).double().numpy())
+            yn, y0 = outs
+            e = yn - y0
+            snr = 10 * np.log10(np.sum(ideal ** 2) / np.sum((ideal - yn) ** 2))
+            rows.append([s, snr, float(e.mean()), float(e.std()), float(np.sqrt(np.mean(y0 ** 2)))])
+        res[key] = rows
+        print(f"noise stats {key}: {n_seeds} seeds in {time.time() - t0:.1f}s; "
+              f"SNR {np.mean([r[1] for r in rows]):.3f} +- {np.std([r[1] for r in rows]):.3f}")
+    return res
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--seeds", type=int, default=256)
+    ap.add_argument("--skip-stats", action="store_true")
+    args = ap.parse_args()
+    _stub_matplotlib()
+    sys.path.insert(0, args.ref)
+    torch.set_num_threads(os.cpu_count())
+    from memintelli.pimpy.memmat_tensor import DPETensor
+    from memintelli.pimpy.data_formats import SlicedData
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    arrays = {}
+    meta = {}
+    for name, spec in CASES.items():
+        t0 = time.time()
+        out = run_case(name, spec, DPETensor, SlicedData)
+        for k, v in out.items():
+            arrays[f"{name}/{k}"] = v
+        meta[name] = {k: v for k, v in spec.items()}
+        print(f"{name}: y {out['y'].shape} in {time.time() - t0:.2f}s")
+    np.savez_compressed(os.path.join(here, "cases.npz"), **arrays)
+    with open(os.path.join(here, "cases.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+    if not args.skip_stats:
+        st = noise_stats(args.seeds, DPETensor, SlicedData)
+        with open(os.path.join(here, "noise_stats.json"), "w") as f:
+            json.dump({"columns": ["seed", "snr_db", "err_mean", "err_std", "y_rms"], **st}, f)
+
+
+if __name__ == "__main__":
+    main()
