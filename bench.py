@@ -1,0 +1,319 @@
+"""Benchmark: CIM Qwen3-0.6B-architecture prefill on B200 (tokens/s), one process per GPU.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Workload: 8 sequences x 2048 token ids, uniform over the 151936-token
+vocabulary (seeded synthetic data), through a random-init Qwen3-0.6B
+architecture (28 layers, hidden 1024, 16/8 heads x 128, SwiGLU 3072) whose
+197 linears (q/k/v/o, gate/up/down x 28 and lm_head) all run on the CIM
+engine: slices [1,1,2,2,2], weight quant_gran (128,128) / paral (32,32),
+input quant_gran (1,128) / paral (1,32), radc 4096, and the device model of
+the reference's Qwen3 example (HGS 1e-5, LGS 1e-8, 4 levels, rdac 4, read
+variation 0.05).  A step is one full prefill forward with loss.  With N GPUs
+every crossbar is sharded across the ranks (strong scaling of one forward).
+
+``--impl reference`` times the CPU restatement of the reference algorithm on
+the host cores on a bounded sample of the same workload and extrapolates to
+the metric's unit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "CIM Qwen3-0.6B-arch prefill tokens/s (8x2048, all 197 linears on the CIM engine)"
+BATCH, SEQ = 8, 2048
+ENGINE = dict(HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0,
+              read_variation=0.05, vnoise=0.0, rdac=4, g_level=4, radc=4096)
+ARCH = dict(hidden=1024, layers=28, heads=16, kv_heads=8, head_dim=128, intermediate=3072, vocab=151936)
+
+# (K, N) of the CIM linears of one decoder layer, and of lm_head
+LAYER_LINEARS = [(1024, 2048), (1024, 1024), (1024, 1024), (2048, 1024), (1024, 3072), (1024, 3072), (3072, 1024)]
+LM_HEAD = (1024, 151936)
+
+
+def ops_per_token():
+    """Slice-pair ops per token: 2 * Kp * Np * Sx * Sy summed over every CIM linear."""
+    pad = lambda v: math.ceil(v / 128) * 128
+    tot = sum(pad(k) * pad(n) for k, n in LAYER_LINEARS) * ARCH["layers"] + pad(LM_HEAD[0]) * pad(LM_HEAD[1])
+    return 2.0 * tot * 25
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline: the oracle (CPU restatement of the reference algorithm), bounded sample
+# ---------------------------------------------------------------------------------------------
+def cpu_sample(tokens: int = 256, head_cols: int = 4096, seed: int = 0):
+    """Time one decoder layer's 7 CIM linears plus a lm_head column slice on `tokens` tokens.
+
+    Returns (seconds, slice_pair_ops) of the sample.  The per-linear work is the
+    reference's _dot_inference arithmetic (fp32 slice-pair crossbar sums, ADC,
+    shift-add, block rescale, read noise) restated with torch's CPU kernels
+    (oracle.cim_oracle.mvm_float_torch); slicing is included.
+    """
+    import torch
+    from oracle import cim_oracle as O
+    rng = np.random.default_rng(seed)
+    eng = O.Engine(**{k: v for k, v in ENGINE.items()})
+    sm = [1, 1, 2, 2, 2]
+    shapes = LAYER_LINEARS + [(LM_HEAD[0], head_cols)]
+    prepared = []
+    for k, n in shapes:
+        w = (rng.standard_normal((k, n)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((tokens, k)).astype(np.float32)
+        prepared.append((x, w))
+    t0 = time.perf_counter()
+    ops = 0.0
+    for x, w in prepared:
+        xs = O.slice_matrix(x, sm, None, (1, 32), (1, 128))
+        ws = O.slice_matrix(w, sm, None, (32, 32), (128, 128))
+        O.mvm_float_torch(xs, ws, eng, seed=seed, noisy=True)
+        ops += 2.0 * x.shape[0] * xs.geom.cols_p * ws.geom.cols_p * 25
+    return time.perf_counter() - t0, ops
+
+
+def cpu_baseline(target_s: float = 12.0):
+    import torch
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    sec, ops = cpu_sample()
+    reps = 1
+    while sec * reps < target_s and reps < 8:
+        s2, _ = cpu_sample(seed=reps)
+        sec += s2
+        reps += 1
+    rate = ops * reps / sec
+    return {"value": rate / ops_per_token(), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{reps}x (one decoder layer's 7 CIM linears + a 1024x4096 lm_head slice, 256 tokens), "
+                      f"torch-CPU restatement of _dot_inference with read noise, extrapolated by slice-pair op "
+                      f"count ({ops_per_token():.3e} ops/token)"}
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ""
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[0]))
+                smax = float(f[1])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------------------------
+def run_reference(args):
+    """--impl reference: the CPU restatement, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    import torch
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_sample(seed=99, tokens=32)
+    times = []
+    ops = 0.0
+    for s in range(args.steps):
+        sec, ops = cpu_sample(seed=s)
+        times.append(sec)
+    rate = ops * len(times) / sum(times)
+    value = rate / ops_per_token()
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "n_cores": cores,
+            "impl": "reference",
+            "config": {"workload": "Qwen3-0.6B-arch CIM prefill 8x2048 (bounded CPU sample per step)",
+                       "global_batch": BATCH, "seq_len": SEQ, "parallelism": "cpu"},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": "per step: one decoder layer's 7 CIM linears + 1024x4096 lm_head slice on "
+                                       "256 tokens (torch-CPU restatement of _dot_inference with read noise), "
+                                       "extrapolated by slice-pair op count"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+
+    from memintelli_flash_b200 import DPETensor
+    from memintelli_flash_b200 import _native as N
+    from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
+
+    torch.manual_seed(1234 + rank)
+    engine = DPETensor(device=dev, **ENGINE)
+    model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev)
+    torch.cuda.synchronize()
+    g = torch.Generator().manual_seed(1)
+    ids_host = torch.randint(0, ARCH["vocab"], (BATCH, SEQ), generator=g).pin_memory()
+    ids = ids_host.to(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        model(ids)
+    barrier()
+    # ---- device-resident timed region
+    engine.launch_log = []
+    launches0 = N.launch_count()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        t_start.record()
+        for _ in range(args.steps):
+            loss = model(ids)
+        t_end.record()
+        barrier()
+    launches = N.launch_count() - launches0
+    ms = t_start.elapsed_time(t_end)
+    log = engine.launch_log
+    engine.launch_log = None
+    mvm_ms = sum(a.elapsed_time(b) for a, b, _, _ in log)
+    mvm_ops = sum(o for _, _, o, _ in log)
+    mvm_adc = sum(e for _, _, _, e in log)
+    ms_t = torch.tensor([ms, mvm_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms, mvm_ms_max = float(ms_t[0]), float(ms_t[1])
+    tokens = BATCH * SEQ * args.steps
+    value = tokens / (ms / 1000.0)
+    # ---- end to end through the public API: host ids in, host loss out, every step
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss_host = model(ids_host.to(dev, non_blocking=True)).item()
+    e1.record()
+    barrier()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_value = tokens / (float(e2e_ms[0]) / 1000.0)
+
+    peaks, peak_kind = load_peaks()
+    achieved = mvm_ops / (mvm_ms / 1000.0) / 1e12 if mvm_ms > 0 else 0.0
+    peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+    clocks = clk.summary()
+    sm_clock = clocks["sm_mhz"] or 1965.0
+    epi_ceiling = 148 * 64 * sm_clock * 1e6 / 1e12   # ADC events (T/s) at 2 issue slots per event
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "config": {"workload": "Qwen3-0.6B-arch CIM prefill, 8x2048 tokens, 197 CIM linears",
+                           "model": "Qwen3-0.6B-arch (random init)", "global_batch": BATCH, "seq_len": SEQ,
+                           "parallelism": f"crossbar-shard{world}" if world > 1 else "single",
+                           "l2": "inputs larger than L2 (3 GB of programmed crossbars per forward)",
+                           "engine": ENGINE},
+                "sliced_mvm_tops": ops_per_token() * BATCH * SEQ * args.steps / (ms / 1000.0) / 1e12,
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak, "traffic": None, "peak_kind": f"bf16 sustained ({peak_kind})",
+                             "kernel": "mvm_kernel (fused crossbar MVM)", "launches": len(log),
+                             "kernel_share": mvm_ms / ms if ms else None,
+                             "epilogue": {"adc_events_per_s": mvm_adc / (mvm_ms / 1000.0) if mvm_ms else 0.0,
+                                          "ceiling_per_s": epi_ceiling * 1e12,
+                                          "frac": (mvm_adc / (mvm_ms / 1000.0)) / (epi_ceiling * 1e12)
+                                          if mvm_ms else 0.0}},
+                "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * SEQ * 8,
+                        "d2h_bytes_per_step": 4},
+                "gpu_launches": int(launches),
+                "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
+                "loss": float(loss_host)}
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    del model
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,180 @@
+/*
+ * memintelli_b200.h -- C ABI of the B200 (sm_100a) compute-in-memory sliced matmul.
+ *
+ * The reference (zhuizhou/memintelli_flash) is pure Python/PyTorch; each entry
+ * point below replaces a torch op chain of its hot path and names it.  All
+ * pointers are device pointers (except the spec structs, which are host
+ * memory read during the call); sizes are elements unless stated; every call
+ * is asynchronous on `stream` and allocates nothing -- the caller owns every
+ * buffer.  Return value: MIB_OK or one of the MIB_ERR_* codes, with a message
+ * available from mib_last_error().
+ *
+ * Data layout in HBM (all row-major, last index fastest):
+ *   operand planes  [S][rows][Kt * pp]   one plane per bit slice, LSB-first;
+ *                    K is split into Kt crossbar tiles of p rows each, every
+ *                    tile padded to pp = round_up(p, 32 bytes / element size)
+ *                    elements with zeros.  Element = the DAC level (inputs) or
+ *                    conductance level (weights) encoded as E4M3 (exact for
+ *                    levels <= 16) or FP16 (exact integers; noisy values).
+ *   tile scales     [Kt][rows] fp32      dequantisation factor of the quant
+ *                    block that holds (row, tile): bmax/(2^(bits-1)-1) for INT,
+ *                    2^(e+2-bits) for block floating point.
+ *   packed codes    [rows][Kp] uint8     two's complement quantised value
+ *                    (all slices of one element), K padded to Kp.
+ *   block max / exp [batch][nbr][nbc] fp32 (SlicedData.max_data / e_bias).
+ */
+#ifndef MEMINTELLI_B200_H
+#define MEMINTELLI_B200_H
+
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MIB_OK 0
+#define MIB_ERR_PARAM 1       /* invalid parameter value  (reference: ValueError)          */
+#define MIB_ERR_SHAPE 2       /* shape / layout mismatch  (reference: ValueError)          */
+#define MIB_ERR_UNSUPPORTED 3 /* configuration not implemented (reference: NotImplementedError) */
+#define MIB_ERR_CUDA 4        /* CUDA runtime or driver error                               */
+#define MIB_ERR_TIMEOUT 5     /* a bounded device-side wait expired (reported by mib_device_status) */
+
+#define MIB_OPERAND_E4M3 0
+#define MIB_OPERAND_FP16 1
+
+#define MIB_MAX_SLICES 8
+#define MIB_MAX_LEVELS 256
+
+/* Bit-slicing and quantisation of one operand (memintelli/pimpy/data_formats.py:21-58, 116-207). */
+typedef struct mib_slice_spec {
+  int32_t n_slices;                       /* S, 1..8                                        */
+  int32_t slice_method[MIB_MAX_SLICES];   /* MSB-first widths, slice_method[0] == 1          */
+  int32_t bfp;                            /* 0: INT (utils.py:44-83), 1: BFP (utils.py:86-128) */
+  int32_t paral[2];                       /* paral_size (rows, cols)                          */
+  int32_t quant_gran[2];                  /* decoded quant_gran, already rounded up to paral  */
+} mib_slice_spec;
+
+/* Crossbar device model (memintelli/pimpy/memmat_tensor.py:30-115). */
+typedef struct mib_device_spec {
+  double hgs, lgs;              /* high / low conductance state                               */
+  int32_t g_level;              /* conductance levels                                         */
+  int32_t rdac;                 /* DAC resolution                                             */
+  int32_t n_radc;               /* 1: uniform ADC; else one entry per weight slice             */
+  int32_t radc[MIB_MAX_SLICES]; /* ADC resolution, LSB-first weight-slice order (list flipped) */
+  double vread;                 /* read voltage                                               */
+  double vnoise;                /* relative voltage noise std                                 */
+  double write_variation;       /* relative write variation std                               */
+  double rate_stuck_hgs, rate_stuck_lgs;
+  int32_t n_read_sigma;         /* 1: uniform read variation; g_level: per level              */
+  float read_sigma[MIB_MAX_LEVELS];
+} mib_device_spec;
+
+/* Output placement: y[(r / rows_per_group) * group_stride + (r % rows_per_group) * row_stride
+ *                     + n * col_stride] for matmul row r and output column n.
+ * Linear (M,N) / (B,T,N): rows_per_group = rows, row_stride = N, col_stride = 1.
+ * Conv NCHW:  rows_per_group = Ho*Wo, group_stride = Cout*Ho*Wo, row_stride = 1, col_stride = Ho*Wo. */
+typedef struct mib_out_layout {
+  int64_t rows_per_group;
+  int64_t group_stride;
+  int64_t row_stride;
+  int64_t col_stride;
+} mib_out_layout;
+
+/* Geometry of the K dimension shared by both operands. */
+typedef struct mib_k_geom {
+  int64_t k;        /* true reduction length                           */
+  int64_t kp;       /* padded length (multiple of both quant blocks)   */
+  int32_t p;        /* crossbar tile depth (input paral[1] == weight paral[0]) */
+  int32_t pp;       /* tile depth padded to the MMA K step             */
+  int64_t kt;       /* number of tiles, kp / p                         */
+} mib_k_geom;
+
+/* Quantise + bit-slice an input matrix (batch, rows, cols) into DAC-level planes.
+ * Replaces SlicedData.slice_data_imp for inputs: data_formats.py:95-114,116-207 with
+ * quant_map_tensor / bfp_map_tensor (utils.py:44-128) and the DAC step of
+ * DPETensor._dot_inference (memmat_tensor.py:295-297 / 358-360).
+ * x[b*ld_batch + r*ld_row + c] (c contiguous).  `packed` may be NULL. */
+int mib_slice_input(const float* x, int64_t batch, int64_t rows, int64_t cols, int64_t ld_batch, int64_t ld_row,
+                    const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                    void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                    cudaStream_t stream);
+
+/* Same for a convolution input (N,C,H,W) lowered without im2col: matmul row
+ * r = n*Ho*Wo + oh*Wo + ow, column c*kh*kw + i*kw + j, the order of F.unfold
+ * used by Conv2dMem (memintelli/NN_layers/convolution.py:105-121). */
+int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
+                         int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
+                         const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                         void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                         cudaStream_t stream);
+
+/* Quantise, slice and program a weight matrix W (K, N) into conductance-level planes.
+ * Replaces SlicedData.slice_data_imp for weights + DPETensor._num2G (memmat_tensor.py:160-202):
+ * level = round(code/m*(g-1)); stuck-at faults from `stuck_field` (torch.rand with the
+ * reference's fixed seed 123, reference G layout (Kp/p0, Np/p1, S, p0, p1)); when
+ * `write_field` (fixed seed 42 draw of N(0, wv), same layout) is given the fp32
+ * conductance planes `g_planes` ([S][N][Kt*pp], siemens, as DPETensor keeps G) are written.
+ * W element (k, n) at w[k*stride_k + n*stride_n]. */
+int mib_program_weight(const float* w, int64_t k, int64_t n, int64_t stride_k, int64_t stride_n,
+                       const mib_slice_spec* spec, const mib_k_geom* kg, const mib_device_spec* dev,
+                       const float* stuck_field, const float* write_field, int32_t operand_kind, void* planes,
+                       float* g_planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                       cudaStream_t stream);
+
+/* Per-call input voltage noise (memmat_tensor.py:297-299): out = level * (1 + vnoise * N(0,1)),
+ * E4M3 level planes in, FP16 planes out; vnoise == 0 converts only.  Counter-based
+ * Philox normals keyed by (seed, call). */
+int mib_input_noise(const uint8_t* planes_e4m3, __half* out_fp16, int64_t n_elems, double vnoise, uint64_t seed,
+                    uint64_t call, cudaStream_t stream);
+
+/* Per-call read variation (memmat_tensor.py:204-236): G' = G * exp(sigma(level) * N(0,1)),
+ * out = (G' - LGS) / Q_G as FP16.  G comes from `g_planes` when non-NULL (write variation
+ * present), else from the E4M3 level planes as level*Q_G + LGS. */
+int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16, int64_t n_elems,
+                          const mib_device_spec* dev, uint64_t seed, uint64_t call, cudaStream_t stream);
+
+/* ADC plan for one MVM configuration.  In the noise-free mode the ADC code
+ * round_half_even(S * (radc_j - 1) / D) must be exact for every reachable
+ * crossbar sum S in [0, D]; when a single fp32 multiply-add cannot guarantee
+ * that (a non-dyadic ratio with half-way ties) the MVM needs a code table of
+ * *table_len_out int32 entries, filled into `table_out` (host memory, may be
+ * NULL) and passed to mib_mvm in device memory.  *mode_out receives the
+ * epilogue variant (bit 0: code table, bit 1: fp32 accumulation).
+ * Mirrors the checks of DPETensor.__init__ / _validate_radc_with_slices
+ * (memmat_tensor.py:98-127). */
+int mib_adc_plan(const mib_slice_spec* x_spec, const mib_slice_spec* w_spec, const mib_k_geom* kg,
+                 const mib_device_spec* dev, int32_t* mode_out, int32_t* table_len_out, int32_t* table_out);
+
+/* Fused crossbar MVM: for every K tile and slice pair, tile partial sums on tcgen05
+ * tensor cores (accumulators in TMEM), ADC round(S * (radc_j-1) / D) with
+ * D = (rdac-1)(g_level-1)p, shift-add over slice pairs, block rescale, K-tile sum
+ * and crop.  Replaces DPETensor.__call__ / MapReduceDot -> _dot_inference / _dot
+ * (memmat_tensor.py:129-158, 260-495; utils.py:11-29).  a_planes [Sx][M][Kt*pp],
+ * a_scale [Kt][M]; b_planes [Sy][N][Kt*pp], b_scale [Kt][N]; both E4M3 or both FP16.
+ * `adc_table` as returned by mib_adc_plan (NULL when none is needed).  `bias` (N)
+ * may be NULL.  `acc_dump`, when non-NULL, receives the exact int32 slice-pair
+ * sums acc[t][r][n] = sum_ij code_ij * m_i m_j c_i c_j of every tile t (test hook). */
+int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_slice_spec* x_spec,
+            const void* b_planes, const float* b_scale, int64_t n, const mib_slice_spec* w_spec,
+            const mib_k_geom* kg, const mib_device_spec* dev, int32_t operand_kind, const int32_t* adc_table,
+            int32_t adc_table_len, float* y, const mib_out_layout* layout, const float* bias, int32_t* acc_dump,
+            cudaStream_t stream);
+
+/* Reads and clears the device-side error flag of the current device (synchronises it).
+ * Returns MIB_OK, or MIB_ERR_TIMEOUT when a kernel gave up a bounded wait. */
+int mib_device_status(void);
+
+/* Message of the last error returned on this thread. */
+const char* mib_last_error(void);
+
+/* Library version string. */
+const char* mib_version(void);
+
+/* Number of CUDA kernels this library has launched in the process (all devices). */
+uint64_t mib_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MEMINTELLI_B200_H */

@@ -1,0 +1,133 @@
+"""ctypes binding of the C ABI in ``include/memintelli_b200.h``.
+
+The library is the only compute path: there is no CPU or PyTorch fallback.
+``lib()`` raises when the shared object has not been built.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+c_i32, c_i64, c_u64, c_f32, c_f64, c_vp = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float,
+                                           ctypes.c_double, ctypes.c_void_p)
+
+MIB_OK = 0
+MIB_ERR_PARAM = 1
+MIB_ERR_SHAPE = 2
+MIB_ERR_UNSUPPORTED = 3
+MIB_ERR_CUDA = 4
+MIB_ERR_TIMEOUT = 5
+
+OPERAND_E4M3 = 0
+OPERAND_FP16 = 1
+
+MODE_LUT = 1
+MODE_FLOATACC = 2
+
+
+class SliceSpec(ctypes.Structure):
+    _fields_ = [("n_slices", c_i32), ("slice_method", c_i32 * 8), ("bfp", c_i32), ("paral", c_i32 * 2),
+                ("quant_gran", c_i32 * 2)]
+
+
+class DeviceSpec(ctypes.Structure):
+    _fields_ = [("hgs", c_f64), ("lgs", c_f64), ("g_level", c_i32), ("rdac", c_i32), ("n_radc", c_i32),
+                ("radc", c_i32 * 8), ("vread", c_f64), ("vnoise", c_f64), ("write_variation", c_f64),
+                ("rate_stuck_hgs", c_f64), ("rate_stuck_lgs", c_f64), ("n_read_sigma", c_i32),
+                ("read_sigma", c_f32 * 256)]
+
+
+class OutLayout(ctypes.Structure):
+    _fields_ = [("rows_per_group", c_i64), ("group_stride", c_i64), ("row_stride", c_i64), ("col_stride", c_i64)]
+
+
+class KGeom(ctypes.Structure):
+    _fields_ = [("k", c_i64), ("kp", c_i64), ("p", c_i32), ("pp", c_i32), ("kt", c_i64)]
+
+
+_P = ctypes.POINTER
+_SIGS = {
+    "mib_slice_input": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, _P(SliceSpec), _P(KGeom), c_i32, c_i32,
+                        c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "mib_slice_conv_input": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                             _P(SliceSpec), _P(KGeom), c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "mib_program_weight": [c_vp, c_i64, c_i64, c_i64, c_i64, _P(SliceSpec), _P(KGeom), _P(DeviceSpec), c_vp, c_vp,
+                           c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "mib_input_noise": [c_vp, c_vp, c_i64, c_f64, c_u64, c_u64, c_vp],
+    "mib_weight_read_noise": [c_vp, c_vp, c_vp, c_i64, _P(DeviceSpec), c_u64, c_u64, c_vp],
+    "mib_adc_plan": [_P(SliceSpec), _P(SliceSpec), _P(KGeom), _P(DeviceSpec), _P(c_i32), _P(c_i32), c_vp],
+    "mib_mvm": [c_vp, c_vp, c_i64, _P(SliceSpec), c_vp, c_vp, c_i64, _P(SliceSpec), _P(KGeom), _P(DeviceSpec), c_i32,
+                c_vp, c_i32, c_vp, _P(OutLayout), c_vp, c_vp, c_vp],
+    "mib_device_status": [],
+}
+EXPORTS = tuple(_SIGS) + ("mib_last_error", "mib_version", "mib_launch_count")
+
+_lock = threading.Lock()
+_lib = None
+
+
+def lib_path() -> str:
+    return _build.LIB
+
+
+def lib():
+    """Load the native library (once).  Raises RuntimeError if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = lib_path()
+            if not os.path.exists(path):
+                raise RuntimeError(f"memintelli_flash_b200 native library not built ({path}); "
+                                   "run `python -m memintelli_flash_b200.build`")
+            L = ctypes.CDLL(path)
+            for name, args in _SIGS.items():
+                fn = getattr(L, name)
+                fn.argtypes = args
+                fn.restype = c_i32
+            L.mib_last_error.restype = ctypes.c_char_p
+            L.mib_last_error.argtypes = []
+            L.mib_version.restype = ctypes.c_char_p
+            L.mib_version.argtypes = []
+            L.mib_launch_count.restype = ctypes.c_uint64
+            L.mib_launch_count.argtypes = []
+            _lib = L
+    return _lib
+
+
+_EXC = {MIB_ERR_PARAM: ValueError, MIB_ERR_SHAPE: ValueError, MIB_ERR_UNSUPPORTED: NotImplementedError,
+        MIB_ERR_CUDA: RuntimeError, MIB_ERR_TIMEOUT: RuntimeError}
+
+
+def check(rc: int):
+    if rc != MIB_OK:
+        msg = lib().mib_last_error().decode(errors="replace")
+        raise _EXC.get(rc, RuntimeError)(msg)
+
+
+def call(name: str, *args):
+    check(getattr(lib(), name)(*args))
+
+
+def ptr(t):
+    """Device pointer of a tensor (or None)."""
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device=None):
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def launch_count() -> int:
+    """Kernels launched by the native library so far in this process."""
+    return int(lib().mib_launch_count())
+
+
+def device_status():
+    """Raise if a kernel on the current device gave up a bounded wait."""
+    check(lib().mib_device_status())

@@ -1,0 +1,147 @@
+"""Crossbar sharding of CIM linear layers across GPUs (one process per GPU).
+
+The reference runs every crossbar of a layer on one device.  Here a layer's
+weight can be split across the ranks of a ``torch.distributed`` process group
+along whole quantisation blocks, which keeps the result exact:
+
+* column sharding (``ColumnShardedLinearMem``): each rank programs a block of
+  output columns (crossbar columns).  ADC, shift-add, block rescale and K-tile
+  sum are all per output column, so every shard's output is bit-identical to
+  the same columns of the unsharded layer.  The output stays sharded (the next
+  layer consumes it sharded) or is all-gathered.
+* row sharding (``RowShardedLinearMem``): each rank programs a block of input
+  rows (crossbar K tiles).  The K-tile partial sums are added after the ADC in
+  the reference (memmat_tensor.py:401), so the shards' outputs sum to the
+  unsharded result up to fp32 summation order; one all-reduce combines them.
+
+Shard boundaries are multiples of the weight quant block along the split
+dimension (``quant_gran`` rounded up to ``paral_size``), so no quant block
+straddles two ranks.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .NN_layers.linear import LinearMem
+
+
+def shard_bounds(n: int, block: int, world: int, rank: int):
+    """[start, stop) of rank's shard of n items split in whole blocks, as evenly as possible."""
+    nblocks = math.ceil(n / block)
+    base, extra = divmod(nblocks, world)
+    b0 = rank * base + min(rank, extra)
+    b1 = b0 + base + (1 if rank < extra else 0)
+    return min(n, b0 * block), min(n, b1 * block)
+
+
+def _world(group):
+    if group is None and not (dist.is_available() and dist.is_initialized()):
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+class _ShardBase(torch.nn.Module):
+    def __init__(self, engine, weight: torch.Tensor, bias: Optional[torch.Tensor], dim: int, input_slice,
+                 weight_slice, bw_e=None, input_paral_size=(1, 32), weight_paral_size=(32, 32),
+                 input_quant_gran=(1, 32), weight_quant_gran=(32, 32), group=None, device=None):
+        super().__init__()
+        self.group = group
+        world, rank = _world(group)
+        out_f, in_f = weight.shape
+        qg = weight_quant_gran if not isinstance(weight_quant_gran, str) else (in_f, out_f)
+        if dim == 0:   # output columns of W^T == rows of the (out, in) weight
+            blk = math.ceil(qg[1] / weight_paral_size[1]) * weight_paral_size[1]
+            lo, hi = shard_bounds(out_f, blk, world, rank)
+            w_local = weight[lo:hi]
+            b_local = None if bias is None else bias[lo:hi]
+            lin_in, lin_out = in_f, hi - lo
+        else:          # input rows (K) of W^T
+            blk = math.ceil(qg[0] / weight_paral_size[0]) * weight_paral_size[0]
+            xq = input_quant_gran if not isinstance(input_quant_gran, str) else (1, in_f)
+            xblk = math.ceil(xq[1] / input_paral_size[1]) * input_paral_size[1]
+            blk = blk * xblk // math.gcd(blk, xblk)
+            lo, hi = shard_bounds(in_f, blk, world, rank)
+            w_local = weight[:, lo:hi]
+            b_local = None
+            lin_in, lin_out = hi - lo, out_f
+            self.full_bias = None if bias is None else bias.detach().clone()
+        self.lo, self.hi, self.world, self.rank = lo, hi, world, rank
+        self.in_features, self.out_features = in_f, out_f
+        self.local = _LinearFromWeight(engine, w_local, b_local, input_slice, weight_slice, bw_e, input_paral_size,
+                                       weight_paral_size, input_quant_gran, weight_quant_gran, device)
+
+    def prepare_for_inference(self):
+        self.local.inference_mode = True
+        self.local.weight_sliced.inference = True
+
+
+class _LinearFromWeight(LinearMem):
+    """LinearMem programmed from a given weight (no random init, programmed once)."""
+
+    def __init__(self, engine, weight, bias, input_slice, weight_slice, bw_e, input_paral_size, weight_paral_size,
+                 input_quant_gran, weight_quant_gran, device):
+        torch.nn.Module.__init__(self)
+        self.in_features = weight.shape[1]
+        self.out_features = weight.shape[0]
+        self.weight = torch.nn.Parameter(weight.detach().to(device=device, dtype=torch.float32).contiguous(),
+                                         requires_grad=False)
+        if bias is not None:
+            self.bias = torch.nn.Parameter(bias.detach().to(device=device, dtype=torch.float32).contiguous(),
+                                           requires_grad=False)
+        else:
+            self.register_parameter('bias', None)
+        from .pimpy.data_formats import SlicedData
+        self.weight_slice_method = torch.tensor(weight_slice)
+        self.input_slice_method = torch.tensor(input_slice)
+        self.weight_sliced = SlicedData(self.weight_slice_method, device=device, bw_e=bw_e, is_weight=True,
+                                        paral_size=weight_paral_size, quant_gran=weight_quant_gran, inference=True)
+        self.engine = engine
+        self.weight_sliced.slice_data_imp(engine, self.weight.detach().t())
+        self.input_paral_size = input_paral_size
+        self.input_quant_gran = input_quant_gran
+        self.inference_mode = True
+
+
+class ColumnShardedLinearMem(_ShardBase):
+    """Output columns split across ranks; ``forward`` returns this rank's columns
+    (``gather=True``: all-gathers the full output along the last dimension)."""
+
+    def __init__(self, engine, weight, bias, input_slice, weight_slice, gather=False, **kw):
+        super().__init__(engine, weight, bias, 0, input_slice, weight_slice, **kw)
+        self.gather = gather
+        qg = kw.get("weight_quant_gran", (32, 32))
+        wp = kw.get("weight_paral_size", (32, 32))
+        blk = math.ceil(qg[1] / wp[1]) * wp[1] if not isinstance(qg, str) else self.out_features
+        self.shard_sizes = [b - a for a, b in (shard_bounds(self.out_features, blk, self.world, r)
+                                               for r in range(self.world))]
+
+    def forward(self, x):
+        y = self.local(x)
+        if not self.gather or self.world == 1:
+            return y
+        width = max(self.shard_sizes)
+        if y.shape[-1] < width:
+            y = torch.nn.functional.pad(y, (0, width - y.shape[-1]))
+        parts = [torch.empty_like(y) for _ in range(self.world)]
+        dist.all_gather(parts, y.contiguous(), group=self.group)
+        return torch.cat([p[..., :n] for p, n in zip(parts, self.shard_sizes)], dim=-1)
+
+
+class RowShardedLinearMem(_ShardBase):
+    """Input rows (K) split across ranks; ``forward`` takes this rank's slice of
+    the input features and all-reduces the partial outputs."""
+
+    def __init__(self, engine, weight, bias, input_slice, weight_slice, **kw):
+        super().__init__(engine, weight, bias, 1, input_slice, weight_slice, **kw)
+
+    def forward(self, x_local):
+        y = self.local(x_local)
+        if self.world > 1:
+            dist.all_reduce(y, group=self.group)
+        if self.full_bias is not None:
+            y = y + self.full_bias.to(y.device)
+        return y

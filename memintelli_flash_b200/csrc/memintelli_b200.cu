@@ -1,0 +1,534 @@
+// C ABI of the B200 CIM sliced matmul (declared in include/memintelli_b200.h).
+//
+// One translation unit: the kernel sources are included here so the device
+// error flag and the kernels share a module.  This layer validates arguments
+// with the reference's error semantics, derives the kernel parameter blocks,
+// encodes the TMA tensor maps and launches.  It never allocates memory.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <string>
+
+#include "slice.cu"
+#include "mvm.cu"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(MIB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+struct SliceTab {
+  int S = 0, bits = 0;
+  int widths[8] = {}, offs[8] = {}, maxes[8] = {};
+  long long coef[8] = {};  // shift weight c_t (LSB-first, sign slice negative)
+};
+
+// memintelli/pimpy/data_formats.py:45-46, 60-71
+int make_tab(const mib_slice_spec* sp, SliceTab& t) {
+  if (!sp) return fail(MIB_ERR_PARAM, "slice spec is NULL");
+  if (sp->n_slices < 1 || sp->n_slices > MIB_MAX_SLICES)
+    return fail(MIB_ERR_PARAM, "number of slices must be in [1, 8]");
+  if (sp->slice_method[0] != 1) return fail(MIB_ERR_PARAM, "The first bit of the slice method should be 1");
+  t.S = sp->n_slices;
+  int off = 0;
+  for (int i = 0; i < t.S; ++i) {
+    const int w = sp->slice_method[t.S - 1 - i];
+    if (w < 1 || w > 8) return fail(MIB_ERR_PARAM, "slice widths must be in [1, 8]");
+    t.widths[i] = w;
+    t.offs[i] = off;
+    t.maxes[i] = (1 << w) - 1;
+    t.coef[i] = 1ll << off;
+    off += w;
+  }
+  t.coef[t.S - 1] = -t.coef[t.S - 1];
+  t.bits = off;
+  if (t.bits > 8) return fail(MIB_ERR_UNSUPPORTED, "total slice width above 8 bits is not supported");
+  if (t.bits < 2) return fail(MIB_ERR_PARAM, "total slice width must be at least 2 bits");
+  return MIB_OK;
+}
+
+int esize(int kind) { return kind == MIB_OPERAND_E4M3 ? 1 : 2; }
+
+int check_kgeom(const mib_k_geom* kg, int kind) {
+  if (!kg) return fail(MIB_ERR_PARAM, "k geometry is NULL");
+  if (kg->p < 1) return fail(MIB_ERR_PARAM, "crossbar tile depth must be positive");
+  if (kg->pp < kg->p || kg->pp % 4) return fail(MIB_ERR_PARAM, "padded tile depth must be >= p and a multiple of 4");
+  const int rb = kg->pp * esize(kind);
+  if (rb != 32 && rb != 64 && rb != 128)
+    return fail(MIB_ERR_UNSUPPORTED, "padded tile row must be 32, 64 or 128 bytes");
+  if (kg->kt * kg->p != kg->kp || kg->kp < kg->k)
+    return fail(MIB_ERR_SHAPE, "inconsistent K geometry (kp != kt * p or kp < k)");
+  return MIB_OK;
+}
+
+int max_level_for(int kind) { return kind == MIB_OPERAND_E4M3 ? 16 : 2048; }
+
+void fill_slice_args(mib::SliceArgs& a, const SliceTab& t, const mib_slice_spec* sp, const mib_k_geom* kg,
+                     int64_t batch, int64_t rows, int64_t cols, int32_t rdac, int32_t kind, void* planes,
+                     float* tile_scale, float* block_max, float* block_exp, uint8_t* packed) {
+  a.batch = batch;
+  a.rows = rows;
+  a.cols = cols;
+  a.qg0 = sp->quant_gran[0];
+  a.qg1 = sp->quant_gran[1];
+  a.nbr = (rows + a.qg0 - 1) / a.qg0;
+  a.nbc = (cols + a.qg1 - 1) / a.qg1;
+  a.p = kg->p;
+  a.pp = kg->pp;
+  a.kt = kg->kt;
+  a.kp = kg->kp;
+  a.bits = t.bits;
+  a.bfp = sp->bfp ? 1 : 0;
+  a.n_slices = t.S;
+  a.lm1 = rdac - 1;
+  a.kind = kind;
+  for (int i = 0; i < 8; ++i) {
+    a.offs[i] = t.offs[i];
+    a.maxes[i] = t.maxes[i] ? t.maxes[i] : 1;
+  }
+  a.planes = planes;
+  a.row_pitch = kg->kt * kg->pp;
+  a.plane_stride = batch * rows * a.row_pitch;
+  a.tile_scale = tile_scale;
+  a.scale_ld = batch * rows;
+  a.block_max = block_max;
+  a.block_exp = block_exp;
+  a.packed = packed;
+}
+
+int check_input_geom(const SliceTab& t, const mib_slice_spec* sp, const mib_k_geom* kg, int64_t cols, int32_t rdac,
+                     int32_t kind, const void* planes, const float* tile_scale, const float* block_max) {
+  (void)t;
+  if (!planes || !tile_scale || !block_max) return fail(MIB_ERR_PARAM, "output buffer is NULL");
+  if (kind != MIB_OPERAND_E4M3 && kind != MIB_OPERAND_FP16) return fail(MIB_ERR_PARAM, "unknown operand kind");
+  if (int r = check_kgeom(kg, kind)) return r;
+  if (sp->paral[0] < 1 || sp->paral[1] < 1) return fail(MIB_ERR_PARAM, "paral_size must be positive");
+  if (sp->paral[1] != kg->p) return fail(MIB_ERR_SHAPE, "input paral_size[1] must equal the crossbar tile depth");
+  if (sp->quant_gran[0] < 1 || sp->quant_gran[1] < 1 || sp->quant_gran[0] % sp->paral[0] ||
+      sp->quant_gran[1] % sp->paral[1])
+    return fail(MIB_ERR_PARAM, "quant_gran must be a positive multiple of paral_size");
+  const int64_t nbc = (cols + sp->quant_gran[1] - 1) / sp->quant_gran[1];
+  if (nbc * sp->quant_gran[1] != kg->kp) return fail(MIB_ERR_SHAPE, "input K padding does not match the K geometry");
+  if (rdac < 2) return fail(MIB_ERR_PARAM, "The resolution of the DAC should be larger than 1!");
+  if (rdac - 1 > max_level_for(kind))
+    return fail(MIB_ERR_UNSUPPORTED, "DAC levels do not fit the operand type (use FP16 operands)");
+  return MIB_OK;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D map over operand planes [S][rows][kt*pp]; box = one crossbar tile of 128 rows, all slices.
+int encode_planes(CUtensorMap* map, const void* base, int kind, int64_t rows, int64_t row_elems, int slices, int pp) {
+  auto enc = tensor_map_encoder();
+  if (!enc) return fail(MIB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  const int es = esize(kind);
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_elems), static_cast<cuuint64_t>(rows),
+                              static_cast<cuuint64_t>(slices)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_elems * es), static_cast<cuuint64_t>(rows * row_elems * es)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(pp), 128u, static_cast<cuuint32_t>(slices)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const int rb = pp * es;
+  const CUtensorMapSwizzle swz = rb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                          : (rb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+  const CUtensorMapDataType dt = kind == MIB_OPERAND_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof(buf), "cuTensorMapEncodeTiled failed (%d) rows=%lld row_elems=%lld slices=%d pp=%d", int(r),
+             static_cast<long long>(rows), static_cast<long long>(row_elems), slices, pp);
+    return fail(MIB_ERR_CUDA, buf);
+  }
+  return MIB_OK;
+}
+
+// exact round_half_even(num / den) for num >= 0, den > 0
+long long rne_div(long long num, long long den) {
+  long long q = num / den, r = num % den;
+  if (2 * r > den || (2 * r == den && (q & 1))) ++q;
+  return q;
+}
+
+bool noise_free(const mib_device_spec* d) {
+  if (d->vnoise != 0.0 || d->write_variation != 0.0) return false;
+  for (int i = 0; i < std::max(1, d->n_read_sigma); ++i)
+    if (d->read_sigma[i] != 0.0f) return false;
+  return true;
+}
+
+struct AdcPlan {
+  int mode = 0;          // MODE_LUT / MODE_FLOATACC bits
+  int lut_len = 0;       // entries per weight slice
+  float cadc[8] = {};
+  int flush = 1;
+  long long R[8] = {};
+  long long D = 0;
+};
+
+int radc_of(const mib_device_spec* d, int j, int Sy, long long* out) {
+  if (d->n_radc == 1) {
+    *out = d->radc[0];
+  } else {
+    if (d->n_radc != Sy) {
+      char buf[128];
+      snprintf(buf, sizeof(buf), "Length of radc array (%d) must match number of weight slices (%d)", d->n_radc, Sy);
+      return fail(MIB_ERR_PARAM, buf);
+    }
+    *out = d->radc[j];
+  }
+  if (*out < 2) return fail(MIB_ERR_PARAM, "All ADC resolution values should be larger than 1!");
+  return MIB_OK;
+}
+
+// Chooses the ADC code source and the accumulation for one MVM configuration.
+int adc_plan(const SliceTab& tx, const SliceTab& tw, const mib_slice_spec* xs, const mib_slice_spec* wsp,
+             const mib_k_geom* kg, const mib_device_spec* dev, AdcPlan& pl) {
+  const long long D = static_cast<long long>(dev->rdac - 1) * (dev->g_level - 1) * kg->p;
+  pl.D = D;
+  bool uniform = true;
+  for (int j = 0; j < tw.S; ++j) {
+    if (int r = radc_of(dev, j, tw.S, &pl.R[j])) return r;
+    pl.R[j] -= 1;
+    pl.cadc[j] = static_cast<float>(static_cast<double>(pl.R[j]) / static_cast<double>(D));
+    if (pl.R[j] != pl.R[0]) uniform = false;
+  }
+  const bool exact = noise_free(dev);
+  bool need_lut = false;
+  if (exact) {
+    // magic-constant rounding must reproduce the exact half-even code for every reachable S in [0, D]
+    for (int j = 0; j < tw.S && !need_lut; ++j) {
+      for (long long S = 0; S <= D; ++S) {
+        const float t = std::fma(static_cast<float>(S), pl.cadc[j], 12582912.0f) - 12582912.0f;
+        if (static_cast<long long>(t) != rne_div(S * pl.R[j], D)) {
+          need_lut = true;
+          break;
+        }
+      }
+    }
+  }
+  if (need_lut) {
+    pl.mode |= mib::MODE_LUT;
+    pl.lut_len = static_cast<int>(D + 1);
+  }
+  long long wsum = 0;
+  for (int i = 0; i < tx.S; ++i)
+    for (int j = 0; j < tw.S; ++j) wsum += std::llabs(tx.maxes[i] * tw.maxes[j] * tx.coef[i] * tw.coef[j]);
+  long long qmax = 0;
+  for (int j = 0; j < tw.S; ++j) qmax = std::max(qmax, pl.R[j]);
+  if (!exact) qmax *= 2;  // noisy crossbar sums can exceed the nominal full scale
+  const double limit = 0.98 * 2147483648.0;
+  const double per_tile = static_cast<double>(wsum) * static_cast<double>(qmax);
+  if (!uniform || per_tile >= limit) {
+    pl.mode |= mib::MODE_FLOATACC;
+    pl.flush = 1;
+  } else {
+    const long long fmax = static_cast<long long>(limit / per_tile);
+    const long long kx = xs->quant_gran[1] / kg->p, kw = wsp->quant_gran[0] / kg->p;
+    const long long kblk = std::gcd(kx, kw);
+    long long f = 1;
+    for (long long d = 1; d <= kblk; ++d)
+      if (kblk % d == 0 && d <= fmax) f = d;
+    pl.flush = static_cast<int>(f);
+  }
+  return MIB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mib_last_error(void) { return g_err.c_str(); }
+
+const char* mib_version(void) { return "memintelli_b200 0.1.0 (sm_100a)"; }
+
+uint64_t mib_launch_count(void) { return mib::launch_count(); }
+
+int mib_device_status(void) {
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "device synchronize");
+  e = cudaMemcpyFromSymbol(&v, mib::g_device_error, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read device error flag");
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(mib::g_device_error, &zero, sizeof(int));
+    char buf[96];
+    snprintf(buf, sizeof(buf), "a bounded device wait expired (site %d)", v);
+    return fail(MIB_ERR_TIMEOUT, buf);
+  }
+  return MIB_OK;
+}
+
+int mib_slice_input(const float* x, int64_t batch, int64_t rows, int64_t cols, int64_t ld_batch, int64_t ld_row,
+                    const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                    void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                    cudaStream_t stream) {
+  SliceTab t;
+  if (int r = make_tab(spec, t)) return r;
+  if (!x) return fail(MIB_ERR_PARAM, "input is NULL");
+  if (batch < 1 || rows < 1 || cols < 1) return fail(MIB_ERR_SHAPE, "input must be non-empty");
+  if (int r = check_input_geom(t, spec, kg, cols, rdac, operand_kind, planes, tile_scale, block_max)) return r;
+  if (spec->bfp && !block_exp) return fail(MIB_ERR_PARAM, "block floating point needs the exponent buffer");
+  mib::SliceArgs a;
+  fill_slice_args(a, t, spec, kg, batch, rows, cols, rdac, operand_kind, planes, tile_scale, block_max, block_exp,
+                  packed);
+  cudaError_t e = mib::slice_dense(x, ld_batch, ld_row, a, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "slice_input launch");
+  return MIB_OK;
+}
+
+int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
+                         int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
+                         const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                         void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                         cudaStream_t stream) {
+  SliceTab t;
+  if (int r = make_tab(spec, t)) return r;
+  if (!x) return fail(MIB_ERR_PARAM, "input is NULL");
+  if (n < 1 || c < 1 || h < 1 || w < 1 || kh < 1 || kw < 1 || sh < 1 || sw < 1 || dh < 1 || dw < 1 || ph < 0 || pw < 0)
+    return fail(MIB_ERR_SHAPE, "invalid convolution geometry");
+  const int64_t ho = (h + 2 * ph - static_cast<int64_t>(dh) * (kh - 1) - 1) / sh + 1;
+  const int64_t wo = (w + 2 * pw - static_cast<int64_t>(dw) * (kw - 1) - 1) / sw + 1;
+  if (ho < 1 || wo < 1) return fail(MIB_ERR_SHAPE, "convolution output is empty");
+  const int64_t cols = c * kh * kw;
+  if (int r = check_input_geom(t, spec, kg, cols, rdac, operand_kind, planes, tile_scale, block_max)) return r;
+  if (spec->bfp && !block_exp) return fail(MIB_ERR_PARAM, "block floating point needs the exponent buffer");
+  mib::SliceArgs a;
+  fill_slice_args(a, t, spec, kg, n, ho * wo, cols, rdac, operand_kind, planes, tile_scale, block_max, block_exp,
+                  packed);
+  cudaError_t e = mib::slice_conv(x, c, h, w, ho, wo, kh, kw, sh, sw, ph, pw, dh, dw, a, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "slice_conv_input launch");
+  return MIB_OK;
+}
+
+int mib_program_weight(const float* w, int64_t k, int64_t n, int64_t stride_k, int64_t stride_n,
+                       const mib_slice_spec* spec, const mib_k_geom* kg, const mib_device_spec* dev,
+                       const float* stuck_field, const float* write_field, int32_t operand_kind, void* planes,
+                       float* g_planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                       cudaStream_t stream) {
+  SliceTab t;
+  if (int r = make_tab(spec, t)) return r;
+  if (!w || !planes || !tile_scale || !block_max || !dev) return fail(MIB_ERR_PARAM, "NULL argument");
+  if (k < 1 || n < 1) return fail(MIB_ERR_SHAPE, "weight must be non-empty");
+  if (operand_kind != MIB_OPERAND_E4M3 && operand_kind != MIB_OPERAND_FP16)
+    return fail(MIB_ERR_PARAM, "unknown operand kind");
+  if (int r = check_kgeom(kg, operand_kind)) return r;
+  if (spec->paral[0] != kg->p) return fail(MIB_ERR_SHAPE, "weight paral_size[0] must equal the crossbar tile depth");
+  if (spec->paral[1] < 1) return fail(MIB_ERR_PARAM, "paral_size must be positive");
+  if (spec->quant_gran[0] < 1 || spec->quant_gran[1] < 1 || spec->quant_gran[0] % spec->paral[0] ||
+      spec->quant_gran[1] % spec->paral[1])
+    return fail(MIB_ERR_PARAM, "quant_gran must be a positive multiple of paral_size");
+  const int64_t nbr = (k + spec->quant_gran[0] - 1) / spec->quant_gran[0];
+  const int64_t nbc = (n + spec->quant_gran[1] - 1) / spec->quant_gran[1];
+  if (nbr * spec->quant_gran[0] != kg->kp) return fail(MIB_ERR_SHAPE, "weight K padding does not match the K geometry");
+  if (dev->g_level < 2) return fail(MIB_ERR_PARAM, "The number of the conductance levels should be larger than 1!");
+  if (dev->g_level - 1 > max_level_for(operand_kind))
+    return fail(MIB_ERR_UNSUPPORTED, "conductance levels do not fit the operand type (use FP16 operands)");
+  if (!(dev->lgs < dev->hgs))
+    return fail(MIB_ERR_PARAM, "The low conductance state should be smaller than the high conductance state!");
+  if (spec->bfp && !block_exp) return fail(MIB_ERR_PARAM, "block floating point needs the exponent buffer");
+  if (write_field && !g_planes) return fail(MIB_ERR_PARAM, "write variation needs the conductance planes");
+  mib::ProgramArgs a;
+  a.k = k;
+  a.n = n;
+  a.kt = kg->kt;
+  a.kp = kg->kp;
+  a.p = kg->p;
+  a.pp = kg->pp;
+  a.qg0 = spec->quant_gran[0];
+  a.qg1 = spec->quant_gran[1];
+  a.nbr = nbr;
+  a.nbc = nbc;
+  a.bits = t.bits;
+  a.bfp = spec->bfp ? 1 : 0;
+  a.n_slices = t.S;
+  a.g_level = dev->g_level;
+  a.kind = operand_kind;
+  for (int i = 0; i < 8; ++i) {
+    a.offs[i] = t.offs[i];
+    a.maxes[i] = t.maxes[i] ? t.maxes[i] : 1;
+  }
+  const double qg = (dev->hgs - dev->lgs) / (dev->g_level - 1);
+  a.qg_f = static_cast<float>(qg);
+  a.lgs_f = static_cast<float>(dev->lgs);
+  a.hgs_f = static_cast<float>(dev->hgs);
+  a.rate_h = static_cast<float>(dev->rate_stuck_hgs);
+  a.rate_l = static_cast<float>(dev->rate_stuck_lgs);
+  a.rate_hl = static_cast<float>(dev->rate_stuck_hgs + dev->rate_stuck_lgs);
+  a.p0 = spec->paral[0];
+  a.p1 = spec->paral[1];
+  a.np_pad = nbc * spec->quant_gran[1];
+  a.stuck_field = (dev->rate_stuck_hgs > 0 || dev->rate_stuck_lgs > 0) ? stuck_field : nullptr;
+  a.write_field = dev->write_variation > 0 ? write_field : nullptr;
+  a.planes = planes;
+  a.g_planes = g_planes;
+  a.row_pitch = kg->kt * kg->pp;
+  a.tile_scale = tile_scale;
+  a.block_max = block_max;
+  a.block_exp = block_exp;
+  a.packed = packed;
+  cudaError_t e = mib::program_weight(w, stride_k, stride_n, a, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "program_weight launch");
+  return MIB_OK;
+}
+
+int mib_input_noise(const uint8_t* planes_e4m3, __half* out_fp16, int64_t n_elems, double vnoise, uint64_t seed,
+                    uint64_t call, cudaStream_t stream) {
+  if (!planes_e4m3 || !out_fp16) return fail(MIB_ERR_PARAM, "NULL argument");
+  if (n_elems % 8) return fail(MIB_ERR_SHAPE, "element count must be a multiple of 8");
+  cudaError_t e = mib::input_noise(planes_e4m3, out_fp16, n_elems, static_cast<float>(vnoise), seed,
+                                   (call << 2) | 1u, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "input_noise launch");
+  return MIB_OK;
+}
+
+int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16, int64_t n_elems,
+                          const mib_device_spec* dev, uint64_t seed, uint64_t call, cudaStream_t stream) {
+  if ((!planes_e4m3 && !g_planes) || !out_fp16 || !dev) return fail(MIB_ERR_PARAM, "NULL argument");
+  if (n_elems % 4) return fail(MIB_ERR_SHAPE, "element count must be a multiple of 4");
+  mib::ReadNoiseArgs a;
+  memset(&a, 0, sizeof(a));
+  a.qg_f = static_cast<float>((dev->hgs - dev->lgs) / (dev->g_level - 1));
+  a.lgs_f = static_cast<float>(dev->lgs);
+  a.g_level = dev->g_level;
+  const int ns = std::max(1, dev->n_read_sigma);
+  if (ns != 1 && ns != dev->g_level) return fail(MIB_ERR_PARAM, "read variation needs one value or one per level");
+  bool any = false, same = true;
+  for (int i = 0; i < ns; ++i) {
+    a.sigma[i] = dev->read_sigma[i];
+    any = any || dev->read_sigma[i] > 0.0f;
+    same = same && dev->read_sigma[i] == dev->read_sigma[0];
+  }
+  // memmat_tensor.py:218-233: identical sigmas skip the level lookup
+  a.any_sigma = any ? 1 : 0;
+  a.per_level = (any && !same) ? 1 : 0;
+  cudaError_t e = mib::read_noise(planes_e4m3, g_planes, out_fp16, n_elems, a, seed, (call << 2) | 2u, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "read_noise launch");
+  return MIB_OK;
+}
+
+int mib_adc_plan(const mib_slice_spec* x_spec, const mib_slice_spec* w_spec, const mib_k_geom* kg,
+                 const mib_device_spec* dev, int32_t* mode_out, int32_t* table_len_out, int32_t* table_out) {
+  SliceTab tx, tw;
+  if (int r = make_tab(x_spec, tx)) return r;
+  if (int r = make_tab(w_spec, tw)) return r;
+  if (!kg || !dev) return fail(MIB_ERR_PARAM, "NULL argument");
+  AdcPlan pl;
+  if (int r = adc_plan(tx, tw, x_spec, w_spec, kg, dev, pl)) return r;
+  if (mode_out) *mode_out = pl.mode;
+  const int32_t len = (pl.mode & mib::MODE_LUT) ? tw.S * pl.lut_len : 0;
+  if (table_len_out) *table_len_out = len;
+  if (table_out && len) {
+    for (int j = 0; j < tw.S; ++j)
+      for (long long S = 0; S < pl.lut_len; ++S)
+        table_out[j * pl.lut_len + S] = static_cast<int32_t>(rne_div(S * pl.R[j], pl.D));
+  }
+  return MIB_OK;
+}
+
+int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_slice_spec* x_spec,
+            const void* b_planes, const float* b_scale, int64_t n, const mib_slice_spec* w_spec,
+            const mib_k_geom* kg, const mib_device_spec* dev, int32_t operand_kind, const int32_t* adc_table,
+            int32_t adc_table_len, float* y, const mib_out_layout* layout, const float* bias, int32_t* acc_dump,
+            cudaStream_t stream) {
+  SliceTab tx, tw;
+  if (int r = make_tab(x_spec, tx)) return r;
+  if (int r = make_tab(w_spec, tw)) return r;
+  if (!a_planes || !a_scale || !b_planes || !b_scale || !y || !layout || !dev)
+    return fail(MIB_ERR_PARAM, "NULL argument");
+  if (operand_kind != MIB_OPERAND_E4M3 && operand_kind != MIB_OPERAND_FP16)
+    return fail(MIB_ERR_PARAM, "unknown operand kind");
+  if (int r = check_kgeom(kg, operand_kind)) return r;
+  if (m < 1 || n < 1) return fail(MIB_ERR_SHAPE, "empty matmul");
+  if (m > 65535LL * mib::kMvmBM) return fail(MIB_ERR_UNSUPPORTED, "too many rows for one launch");
+  if (x_spec->paral[1] != kg->p || w_spec->paral[0] != kg->p)
+    return fail(MIB_ERR_SHAPE, "The input data mismatches the shape of weight data!");
+  if ((x_spec->bfp != 0) != (w_spec->bfp != 0))
+    return fail(MIB_ERR_PARAM, "input and weight must both be INT or both be block floating point");
+  if (dev->rdac < 2) return fail(MIB_ERR_PARAM, "The resolution of the DAC should be larger than 1!");
+  if (dev->g_level < 2) return fail(MIB_ERR_PARAM, "The number of the conductance levels should be larger than 1!");
+  for (int j = 0; j < tw.S; ++j)
+    if (tw.maxes[j] > dev->g_level - 1) return fail(MIB_ERR_PARAM, "The weight data is out of the range!");
+  AdcPlan pl;
+  if (int r = adc_plan(tx, tw, x_spec, w_spec, kg, dev, pl)) return r;
+  if ((pl.mode & mib::MODE_LUT) && (!adc_table || adc_table_len != tw.S * pl.lut_len))
+    return fail(MIB_ERR_PARAM, "this ADC configuration needs the code table from mib_adc_plan");
+  int mode = pl.mode;
+  if (acc_dump) {
+    if (pl.mode & mib::MODE_FLOATACC)
+      return fail(MIB_ERR_UNSUPPORTED, "tile-sum dump needs a uniform ADC without int32 overflow");
+    mode |= mib::MODE_DUMP;
+  }
+  mib::MvmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.M = m;
+  a.N = n;
+  a.Kt = kg->kt;
+  a.pp = kg->pp;
+  a.Sx = tx.S;
+  a.Sy = tw.S;
+  a.row_bytes = kg->pp * esize(operand_kind);
+  a.a_slice_bytes = static_cast<uint32_t>(mib::kMvmBM * a.row_bytes);
+  a.b_slice_bytes = static_cast<uint32_t>(mib::kMvmBN * a.row_bytes);
+  a.stage_bytes = static_cast<uint32_t>(tx.S) * a.a_slice_bytes + static_cast<uint32_t>(tw.S) * a.b_slice_bytes;
+  a.lut_len = pl.lut_len;
+  a.lut = adc_table;
+  a.lut_smem = (pl.mode & mib::MODE_LUT) && static_cast<size_t>(tw.S) * pl.lut_len * 4 <= 48 * 1024 ? 1 : 0;
+  const size_t budget = 225 * 1024;
+  const size_t fixed = 1024 + sizeof(float) * mib::kMvmBM * mib::kMvmBN + sizeof(mib::SmemCtl) + (a.lut_smem ? static_cast<size_t>(tw.S) * pl.lut_len * 4 : 0);
+  if (fixed + a.stage_bytes > budget) return fail(MIB_ERR_UNSUPPORTED, "one K tile of all slices exceeds shared memory");
+  a.stages = static_cast<int32_t>(std::min<size_t>(8, (budget - fixed) / a.stage_bytes));
+  a.flush_tiles = pl.flush;
+  for (int j = 0; j < 8; ++j) a.cadc[j] = pl.cadc[j];
+  uint32_t off = 0;
+  for (int i = 0; i < tx.S; ++i)
+    for (int j = 0; j < tw.S; ++j) {
+      const long long wij = tx.maxes[i] * tw.maxes[j] * tx.coef[i] * tw.coef[j];
+      a.wpair[i * 8 + j] = static_cast<int32_t>(wij);
+      a.wfpair[i * 8 + j] = static_cast<float>(static_cast<double>(wij) * kg->p / static_cast<double>(pl.R[j]));
+      off += static_cast<uint32_t>(wij) * mib::kMagicBits;
+    }
+  a.tile_offset = off;
+  a.out_scale = static_cast<float>(static_cast<double>(kg->p) / static_cast<double>(pl.R[0]));
+  a.xs = a_scale;
+  a.ws = b_scale;
+  a.y = y;
+  a.rows_per_group = layout->rows_per_group > 0 ? layout->rows_per_group : m;
+  a.group_stride = layout->group_stride;
+  a.row_stride = layout->row_stride;
+  a.col_stride = layout->col_stride;
+  a.bias = bias;
+  a.acc_dump = acc_dump;
+  CUtensorMap ta, tb;
+  if (int r = encode_planes(&ta, a_planes, operand_kind, m, kg->kt * kg->pp, tx.S, kg->pp)) return r;
+  if (int r = encode_planes(&tb, b_planes, operand_kind, n, kg->kt * kg->pp, tw.S, kg->pp)) return r;
+  cudaError_t e = mib::launch_mvm(ta, tb, a, operand_kind, mode, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "mvm launch");
+  return MIB_OK;
+}
+
+}  // extern "C"

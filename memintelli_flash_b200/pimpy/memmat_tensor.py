@@ -1,0 +1,315 @@
+"""``DPETensor``: the crossbar dot-product engine, on B200 kernels.
+
+API mirror of memintelli/pimpy/memmat_tensor.py:25-158: same constructor,
+validation, attributes and ``engine(x_sliced, w_sliced)`` call.  Both of the
+reference's routes (``_dot_inference`` and ``_dot``, memmat_tensor.py:154-157)
+compute the same arithmetic and map to one fused kernel here; the only
+difference between them was the order of random draws.
+
+Noise models:
+* stuck-at and write-variation faults are drawn exactly as the reference
+  draws them: ``torch.rand`` / ``torch.normal`` over the G shape with
+  fixed-seed generators (123 / 42) on the weight's device
+  (memmat_tensor.py:175-197);
+* read variation (per call, per weight cell, shared by all input rows) and
+  voltage noise (per call, per input element and slice, shared by all
+  output columns) come from a counter-based Philox stream whose seed is
+  drawn from torch's default CPU generator, so ``torch.manual_seed``
+  reproduces a run.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _native as N
+from .data_formats import SlicedData, _decode_gran, padded_tile
+
+
+class DPETensor(object):
+    """Dot-product engine with bit-sliced crossbar arithmetic (memmat_tensor.py:25-115)."""
+
+    def __init__(self, HGS=1e-5, LGS=1e-7, g_level=16, write_variation=0.02, read_variation=0.02,
+                 vnoise=0.05, wire_resistance=0, rdac=2 ** 4, radc=2 ** 8, vread=0.2,
+                 rate_stuck_HGS=0.001, rate_stuck_LGS=0.000,
+                 device=torch.device("cuda:0" if torch.cuda.is_available() else "cpu")):
+        self.HGS = HGS
+        self.LGS = LGS
+        self.g_level = g_level
+        self.write_variation = write_variation
+        if isinstance(read_variation, dict):
+            if set(read_variation.keys()) != set(range(g_level)):
+                raise ValueError(f'read_variation dict must have keys for all g levels 0 to {g_level-1}')
+            self.read_variation = read_variation
+        elif isinstance(read_variation, (int, float)):
+            self.read_variation = {i: read_variation for i in range(g_level)}
+        else:
+            raise ValueError('read_variation must be a dict, float, or None')
+        self.vnoise = vnoise
+        self.rdac = rdac
+        if isinstance(radc, (list, tuple)):
+            self.radc = torch.tensor(radc).flip(0)
+            self.radc_is_list = True
+        else:
+            self.radc = radc
+            self.radc_is_list = False
+        self.vread = vread
+        self.wire_resistance = wire_resistance
+        self.rate_stuck_HGS = rate_stuck_HGS
+        self.rate_stuck_LGS = rate_stuck_LGS
+        self.device = torch.device(device) if not isinstance(device, torch.device) else device
+
+        if self.radc_is_list:
+            if torch.any(self.radc < 2):
+                raise ValueError('All ADC resolution values should be larger than 1!')
+        else:
+            if self.radc < 2:
+                raise ValueError('The resolution of the ADC should be larger than 1!')
+        if self.rdac < 2:
+            raise ValueError('The resolution of the DAC should be larger than 1!')
+        if self.g_level < 2:
+            raise ValueError('The number of the conductance levels should be larger than 1!')
+        if self.LGS >= self.HGS:
+            raise ValueError('The low conductance state should be smaller than the high conductance state!')
+        if self.rate_stuck_HGS + self.rate_stuck_LGS > 1:
+            raise ValueError('The sum of stuck fault rates should not exceed 1!')
+        if self.g_level > 256:
+            raise NotImplementedError('more than 256 conductance levels are not supported')
+
+        self.Q_G = (self.HGS - self.LGS) / (self.g_level - 1)
+        self.conductance_levels = torch.tensor([self.LGS + i * self.Q_G for i in range(self.g_level)])
+        # Device on which the fixed-seed fault fields are drawn; None = the weight's device,
+        # as in the reference.  Tests set "cpu" to reproduce a CPU reference run's faults.
+        self.fault_field_device = None
+        self._plans = {}
+        # When a list, every fused MVM launch appends (start_event, end_event, slice_pair_ops,
+        # adc_events) recorded on the launching stream (used by the benchmark's roofline).
+        self.launch_log = None
+
+    # ------------------------------------------------------------------ specs
+    @property
+    def operand_kind(self) -> int:
+        return N.OPERAND_E4M3 if (self.rdac - 1 <= 16 and self.g_level - 1 <= 16) else N.OPERAND_FP16
+
+    def _sigmas(self):
+        return [float(self.read_variation[i]) for i in range(self.g_level)]
+
+    @property
+    def noisy(self) -> bool:
+        return self.vnoise > 0 or self.write_variation > 0 or any(s > 0 for s in self._sigmas())
+
+    def _device_spec(self) -> N.DeviceSpec:
+        d = N.DeviceSpec()
+        d.hgs, d.lgs = float(self.HGS), float(self.LGS)
+        d.g_level, d.rdac = int(self.g_level), int(self.rdac)
+        if self.radc_is_list:
+            vals = [int(v) for v in self.radc.tolist()]
+            d.n_radc = len(vals)
+            if len(vals) > 8:
+                raise ValueError('at most 8 ADC resolutions are supported')
+            for i, v in enumerate(vals):
+                d.radc[i] = v
+        else:
+            d.n_radc = 1
+            d.radc[0] = int(self.radc)
+        d.vread, d.vnoise, d.write_variation = float(self.vread), float(self.vnoise), float(self.write_variation)
+        d.rate_stuck_hgs, d.rate_stuck_lgs = float(self.rate_stuck_HGS), float(self.rate_stuck_LGS)
+        sig = self._sigmas()
+        if all(s == sig[0] for s in sig):
+            d.n_read_sigma = 1
+            d.read_sigma[0] = sig[0]
+        else:
+            d.n_read_sigma = len(sig)
+            for i, s in enumerate(sig):
+                d.read_sigma[i] = s
+        return d
+
+    def _validate_radc_with_slices(self, mat: SlicedData):
+        """memmat_tensor.py:117-127."""
+        if self.radc_is_list and len(self.radc) != len(mat):
+            raise ValueError(f'Length of radc array ({len(self.radc)}) must match number of weight slices ({len(mat)})')
+
+    # ------------------------------------------------------------ slicing
+    def _k_geom(self, K, qg_k, p, kind):
+        kp = math.ceil(K / qg_k) * qg_k
+        return dict(k=K, kp=kp, p=p, pp=padded_tile(p, kind), kt=kp // p)
+
+    def _slice_input(self, sd: SlicedData, data: torch.Tensor):
+        squeeze = data.dim() == 2
+        x = data.unsqueeze(0) if squeeze else data
+        if x.stride(-1) != 1:
+            x = x.contiguous()
+        B, T, K = x.shape
+        qg = _decode_gran(sd.quant_gran, sd.paral_size, T, K)
+        kind = self.operand_kind
+        geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
+        self._run_input_slicing(sd, kind, geom, qg, B, T, K, squeeze, lambda spec, kg, bufs: N.call(
+            "mib_slice_input", N.ptr(x), B, T, K, x.stride(0), x.stride(1), spec, kg, int(self.rdac), kind,
+            *bufs, N.stream_ptr(x.device)))
+
+    def _slice_conv_input(self, sd: SlicedData, x: torch.Tensor, kernel_size, stride, padding, dilation):
+        x = x.contiguous()
+        n, c, h, w = x.shape
+        kh, kw = kernel_size
+        sh, sw = stride
+        ph, pw = padding
+        dh, dw = dilation
+        ho = (h + 2 * ph - dh * (kh - 1) - 1) // sh + 1
+        wo = (w + 2 * pw - dw * (kw - 1) - 1) // sw + 1
+        T, K = ho * wo, c * kh * kw
+        qg = _decode_gran(sd.quant_gran, sd.paral_size, T, K)
+        kind = self.operand_kind
+        geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
+        self._run_input_slicing(sd, kind, geom, qg, n, T, K, False, lambda spec, kg, bufs: N.call(
+            "mib_slice_conv_input", N.ptr(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg,
+            int(self.rdac), kind, *bufs, N.stream_ptr(x.device)))
+        sd.shape = torch.Size((n, T, K))
+
+    def _run_input_slicing(self, sd, kind, geom, qg, B, T, K, squeeze, launch):
+        dev = self.device
+        S = len(sd.slice_method)
+        rows = B * T
+        nbr = math.ceil(T / qg[0])
+        nbc = math.ceil(K / qg[1])
+        geom.update(batch=B, rows=T, squeeze=squeeze, qg=qg, nbr=nbr, nbc=nbc,
+                    rows_p=nbr * qg[0], cols_p=nbc * qg[1])
+        pdt = torch.uint8 if kind == N.OPERAND_E4M3 else torch.float16
+        planes = torch.empty((S, rows, geom["kt"] * geom["pp"]), dtype=pdt, device=dev)
+        tile_scale = torch.empty((geom["kt"], rows), dtype=torch.float32, device=dev)
+        block_max = torch.empty((B, nbr, nbc), dtype=torch.float32, device=dev)
+        block_exp = torch.empty((B, nbr, nbc), dtype=torch.float32, device=dev) if sd.bw_e else None
+        packed = None if sd.inference else torch.empty((rows, geom["kp"]), dtype=torch.uint8, device=dev)
+        sd._buf = dict(geom=geom, kind=kind, planes=planes, tile_scale=tile_scale, block_max=block_max,
+                       block_exp=block_exp, packed=packed, rdac=int(self.rdac))
+        launch(sd._spec(), sd._kgeom(), (N.ptr(planes), N.ptr(tile_scale), N.ptr(block_max), N.ptr(block_exp),
+                                         N.ptr(packed)))
+
+    def _fault_fields(self, g_shape, device):
+        fdev = torch.device(self.fault_field_device) if self.fault_field_device is not None else device
+        stuck = write = None
+        if self.write_variation > 0:
+            gen = torch.Generator(device=fdev)
+            gen.manual_seed(42)
+            write = torch.normal(0, self.write_variation, g_shape, generator=gen, device=fdev).to(device)
+        if self.rate_stuck_HGS > 0 or self.rate_stuck_LGS > 0:
+            gen = torch.Generator(device=fdev)
+            gen.manual_seed(123)
+            stuck = torch.rand(g_shape, generator=gen, device=fdev).to(device)
+        return stuck, write
+
+    def _program_weight(self, sd: SlicedData, w: torch.Tensor):
+        K, Nc = w.shape
+        dev = self.device
+        qg = _decode_gran(sd.quant_gran, sd.paral_size, K, Nc)
+        p0, p1 = int(sd.paral_size[0]), int(sd.paral_size[1])
+        kind = self.operand_kind
+        geom = self._k_geom(K, qg[0], p0, kind)
+        nbr, nbc = math.ceil(K / qg[0]), math.ceil(Nc / qg[1])
+        S = len(sd.slice_method)
+        geom.update(n=Nc, squeeze=True, qg=qg, nbr=nbr, nbc=nbc, rows_p=nbr * qg[0], cols_p=nbc * qg[1], batch=1)
+        g_shape = (geom["rows_p"] // p0, geom["cols_p"] // p1, S, p0, p1)
+        stuck, write = self._fault_fields(g_shape, w.device)
+        pdt = torch.uint8 if kind == N.OPERAND_E4M3 else torch.float16
+        planes = torch.empty((S, Nc, geom["kt"] * geom["pp"]), dtype=pdt, device=dev)
+        g_planes = torch.empty((S, Nc, geom["kt"] * geom["pp"]), dtype=torch.float32, device=dev) \
+            if write is not None else None
+        tile_scale = torch.empty((geom["kt"], Nc), dtype=torch.float32, device=dev)
+        block_max = torch.empty((nbr, nbc), dtype=torch.float32, device=dev)
+        block_exp = torch.empty((nbr, nbc), dtype=torch.float32, device=dev) if sd.bw_e else None
+        packed = None if sd.inference else torch.empty((Nc, geom["kp"]), dtype=torch.uint8, device=dev)
+        sd._buf = dict(geom=geom, kind=kind, planes=planes, g_planes=g_planes, tile_scale=tile_scale,
+                       block_max=block_max, block_exp=block_exp, packed=packed,
+                       engine=dict(g_level=int(self.g_level), QG32=float(torch.tensor(self.Q_G, dtype=torch.float32)),
+                                   LGS32=float(torch.tensor(self.LGS, dtype=torch.float32)),
+                                   HGS=self.HGS, LGS=self.LGS, wv=self.write_variation,
+                                   stuck=(self.rate_stuck_HGS, self.rate_stuck_LGS)))
+        N.call("mib_program_weight", N.ptr(w), K, Nc, w.stride(0), w.stride(1), sd._spec(), sd._kgeom(),
+               self._device_spec(), N.ptr(stuck), N.ptr(write), kind, N.ptr(planes), N.ptr(g_planes),
+               N.ptr(tile_scale), N.ptr(block_max), N.ptr(block_exp), N.ptr(packed), N.stream_ptr(w.device))
+        del stuck, write
+
+    # ------------------------------------------------------------- the dot
+    def __call__(self, x: SlicedData, mat: SlicedData):
+        return self.MapReduceDot(x, mat)
+
+    def MapReduceDot(self, x: SlicedData, mat: SlicedData, out=None, bias=None, layout=None, acc_dump=None):
+        """Crossbar matmul of a sliced input and a programmed weight (memmat_tensor.py:132-158).
+
+        Returns fp32 (M, N) for a 2-D input, (B, T, N) for a 3-D one.
+        """
+        if mat.device.type != x.device.type:
+            raise ValueError('The input data and weight data should be in the same device!')
+        if x.shape[-1] != mat.shape[-2]:
+            raise ValueError('The input data mismatches the shape of weight data!')
+        self._validate_radc_with_slices(mat)
+        if self.wire_resistance > 0:
+            raise NotImplementedError('The wire_factor is not supported in the training version!')
+        return self._mvm(x, mat, out=out, bias=bias, layout=layout, acc_dump=acc_dump)
+
+    def _plan(self, xs: N.SliceSpec, ws: N.SliceSpec, kg: N.KGeom, dspec: N.DeviceSpec, device):
+        key = (bytes(xs), bytes(ws), bytes(kg), bytes(dspec), str(device))
+        if key not in self._plans:
+            mode, n = N.c_i32(0), N.c_i32(0)
+            N.call("mib_adc_plan", xs, ws, kg, dspec, mode, n, None)
+            table = None
+            if n.value:
+                host = (N.c_i32 * n.value)()
+                N.call("mib_adc_plan", xs, ws, kg, dspec, mode, n, host)
+                table = torch.tensor(list(host), dtype=torch.int32).to(device)
+            self._plans[key] = (mode.value, table, n.value)
+        return self._plans[key]
+
+    def _mvm(self, x: SlicedData, mat: SlicedData, out=None, bias=None, layout=None, acc_dump=None):
+        if x._buf is None or mat._buf is None:
+            raise ValueError('slice_data_imp must be called on both operands first')
+        if x._buf.get("views_only") or mat._buf.get("views_only"):
+            raise ValueError('transposed SlicedData copies carry views only and cannot be multiplied')
+        if not mat.is_weight:
+            raise ValueError('the second operand must be a programmed weight (is_weight=True)')
+        if x._buf.get("rdac") != int(self.rdac) or mat._buf["engine"]["g_level"] != int(self.g_level):
+            raise ValueError('operands were sliced with a different engine configuration')
+        gx, gw = x._buf["geom"], mat._buf["geom"]
+        if gx["kp"] != gw["kp"] or gx["p"] != gw["p"] or x._buf["kind"] != mat._buf["kind"]:
+            raise ValueError('The input data mismatches the shape of weight data!')
+        if max(float(v) for v in mat.sliced_max_weights) > self.g_level - 1:
+            raise ValueError('The weight data is out of the range!')
+        dev = x._buf["planes"].device
+        M = gx["batch"] * gx["rows"]
+        Nc = gw["n"]
+        S_x, S_w = len(x.slice_method), len(mat.slice_method)
+        xs, ws, kg = x._spec(), mat._spec(), x._kgeom()
+        dspec = self._device_spec()
+        stream = N.stream_ptr(dev)
+        kind = x._buf["kind"]
+        a_planes, b_planes = x._buf["planes"], mat._buf["planes"]
+        if self.noisy:
+            if kind != N.OPERAND_E4M3:
+                raise NotImplementedError('noisy crossbars with more than 16 DAC / conductance levels')
+            seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+            a16 = torch.empty(a_planes.shape, dtype=torch.float16, device=dev)
+            b16 = torch.empty(b_planes.shape, dtype=torch.float16, device=dev)
+            N.call("mib_input_noise", N.ptr(a_planes), N.ptr(a16), a_planes.numel(), float(self.vnoise), seed, 0,
+                   stream)
+            N.call("mib_weight_read_noise", N.ptr(b_planes), N.ptr(mat._buf.get("g_planes")), N.ptr(b16),
+                   b_planes.numel(), dspec, seed, 0, stream)
+            a_planes, b_planes, kind = a16, b16, N.OPERAND_FP16
+        mode, table, tlen = self._plan(xs, ws, kg, dspec, dev)
+        if out is None:
+            shape = (M, Nc) if gx["squeeze"] else (gx["batch"], gx["rows"], Nc)
+            out = torch.empty(shape, dtype=torch.float32, device=dev)
+        if layout is None:
+            layout = N.OutLayout(M, 0, Nc, 1)
+        log = self.launch_log
+        if log is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        N.call("mib_mvm", N.ptr(a_planes), N.ptr(x._buf["tile_scale"]), M, xs, N.ptr(b_planes),
+               N.ptr(mat._buf["tile_scale"]), Nc, ws, kg, dspec, kind, N.ptr(table), tlen, N.ptr(out), layout,
+               N.ptr(bias), N.ptr(acc_dump), stream)
+        if log is not None:
+            ev1.record()
+            np_cols = gw["cols_p"]
+            log.append((ev0, ev1, 2.0 * M * gx["kp"] * np_cols * S_x * S_w, float(M) * np_cols * gx["kt"] * S_x * S_w))
+        return out

@@ -1,0 +1,182 @@
+"""Qwen3-0.6B-architecture prefill with every linear on the CIM engine.
+
+The reference wraps a Hugging Face ``AutoModelForCausalLM`` and swaps every
+``nn.Linear`` (q/k/v/o, gate/up/down of 28 layers, and ``lm_head``) for
+``LinearMem`` (memintelli/NN_models/Qwen3.py:82-106); attention, RMSNorm,
+RoPE and SiLU stay in torch.  This module is the same computation written
+compactly so that its crossbars can be sharded across GPUs:
+
+* q/k/v and gate/up are column-sharded (whole heads / whole 128-column quant
+  blocks per rank, outputs stay sharded); o_proj and down_proj are
+  row-sharded, with one all-reduce each;
+* lm_head is column-sharded and the cross-entropy is computed without
+  gathering the logits (distributed log-sum-exp).
+
+With a world size of 1 there is no collective and no sharding.  The
+non-CIM parts (embedding, RMSNorm, RoPE, attention, SiLU, loss) run in torch;
+attention runs in bf16 through scaled_dot_product_attention.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from .crossbar_shard import ColumnShardedLinearMem, RowShardedLinearMem, shard_bounds
+
+
+@dataclass
+class Qwen3Arch:
+    hidden: int = 1024
+    layers: int = 28
+    heads: int = 16
+    kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 3072
+    vocab: int = 151936
+    rope_theta: float = 1e6
+    eps: float = 1e-6
+
+
+@dataclass
+class CimSpec:
+    """Slicing / granularity of every CIM linear (config: weight (128,128)/(32,32), input (1,128)/(1,32))."""
+    input_slice: tuple = (1, 1, 2, 2, 2)
+    weight_slice: tuple = (1, 1, 2, 2, 2)
+    bw_e: object = None
+    input_paral_size: tuple = (1, 32)
+    weight_paral_size: tuple = (32, 32)
+    input_quant_gran: tuple = (1, 128)
+    weight_quant_gran: tuple = (128, 128)
+
+    def kwargs(self):
+        return dict(bw_e=self.bw_e, input_paral_size=self.input_paral_size,
+                    weight_paral_size=self.weight_paral_size, input_quant_gran=self.input_quant_gran,
+                    weight_quant_gran=self.weight_quant_gran)
+
+
+def rms_norm(x, w, eps):
+    v = x.float().pow(2).mean(-1, keepdim=True)
+    return x * torch.rsqrt(v + eps) * w
+
+
+def rope_cache(T, dim, theta, device):
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, device=device, dtype=torch.float64) / dim))
+    t = torch.arange(T, device=device, dtype=torch.float64)
+    f = torch.outer(t, inv)
+    emb = torch.cat([f, f], dim=-1)
+    return emb.cos().float(), emb.sin().float()
+
+
+def apply_rope(x, cos, sin):
+    h = x.shape[-1] // 2
+    rot = torch.cat([-x[..., h:], x[..., :h]], dim=-1)
+    return x * cos + rot * sin
+
+
+class Qwen3CimLayer(torch.nn.Module):
+    def __init__(self, arch: Qwen3Arch, engine, spec: CimSpec, gen: torch.Generator, device, group=None):
+        super().__init__()
+        a = arch
+        self.arch = a
+        std = 0.02
+
+        def w(o, i):
+            return torch.randn(o, i, generator=gen, device=device) * std
+
+        kw = dict(group=group, device=device, **spec.kwargs())
+        sl = (spec.input_slice, spec.weight_slice)
+        self.q_proj = ColumnShardedLinearMem(engine, w(a.heads * a.head_dim, a.hidden), None, *sl, **kw)
+        self.k_proj = ColumnShardedLinearMem(engine, w(a.kv_heads * a.head_dim, a.hidden), None, *sl, **kw)
+        self.v_proj = ColumnShardedLinearMem(engine, w(a.kv_heads * a.head_dim, a.hidden), None, *sl, **kw)
+        self.o_proj = RowShardedLinearMem(engine, w(a.hidden, a.heads * a.head_dim), None, *sl, **kw)
+        self.gate_proj = ColumnShardedLinearMem(engine, w(a.intermediate, a.hidden), None, *sl, **kw)
+        self.up_proj = ColumnShardedLinearMem(engine, w(a.intermediate, a.hidden), None, *sl, **kw)
+        self.down_proj = RowShardedLinearMem(engine, w(a.hidden, a.intermediate), None, *sl, **kw)
+        self.in_norm = torch.nn.Parameter(torch.ones(a.hidden, device=device), requires_grad=False)
+        self.post_norm = torch.nn.Parameter(torch.ones(a.hidden, device=device), requires_grad=False)
+        self.q_norm = torch.nn.Parameter(torch.ones(a.head_dim, device=device), requires_grad=False)
+        self.k_norm = torch.nn.Parameter(torch.ones(a.head_dim, device=device), requires_grad=False)
+        self.local_heads = self.q_proj.local.out_features // a.head_dim
+        self.local_kv = self.k_proj.local.out_features // a.head_dim
+
+    def forward(self, h, cos, sin):
+        a = self.arch
+        B, T, _ = h.shape
+        x = rms_norm(h, self.in_norm, a.eps)
+        q = self.q_proj(x).view(B, T, self.local_heads, a.head_dim)
+        k = self.k_proj(x).view(B, T, self.local_kv, a.head_dim)
+        v = self.v_proj(x).view(B, T, self.local_kv, a.head_dim)
+        q = apply_rope(rms_norm(q, self.q_norm, a.eps), cos, sin).transpose(1, 2)
+        k = apply_rope(rms_norm(k, self.k_norm, a.eps), cos, sin).transpose(1, 2)
+        v = v.transpose(1, 2)
+        o = F.scaled_dot_product_attention(q.bfloat16(), k.bfloat16(), v.bfloat16(), is_causal=True,
+                                           enable_gqa=self.local_heads != self.local_kv)
+        o = o.transpose(1, 2).reshape(B, T, self.local_heads * a.head_dim).float()
+        h = h + self.o_proj(o)
+        x = rms_norm(h, self.post_norm, a.eps)
+        m = F.silu(self.gate_proj(x)) * self.up_proj(x)
+        return h + self.down_proj(m)
+
+
+class Qwen3CimPrefill(torch.nn.Module):
+    """Random-init Qwen3-architecture model; ``forward(ids)`` returns the mean next-token loss."""
+
+    def __init__(self, engine, arch: Qwen3Arch = Qwen3Arch(), spec: CimSpec = CimSpec(), seed: int = 0,
+                 device=None, group=None):
+        super().__init__()
+        device = device or engine.device
+        self.arch, self.group = arch, group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
+        gen = torch.Generator(device=device)
+        gen.manual_seed(seed)
+        self.embed = torch.nn.Parameter(torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02,
+                                        requires_grad=False)
+        self.layers = torch.nn.ModuleList(
+            Qwen3CimLayer(arch, engine, spec, gen, device, group) for _ in range(arch.layers))
+        self.norm = torch.nn.Parameter(torch.ones(arch.hidden, device=device), requires_grad=False)
+        w_head = torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02
+        self.lm_head = ColumnShardedLinearMem(engine, w_head, None, spec.input_slice, spec.weight_slice,
+                                              group=group, device=device, **spec.kwargs())
+        del w_head
+        self._rope = {}
+
+    def cim_linears(self):
+        for layer in self.layers:
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+                yield getattr(layer, name).local
+        yield self.lm_head.local
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        a = self.arch
+        B, T = ids.shape
+        if T not in self._rope:
+            self._rope[T] = rope_cache(T, a.head_dim, a.rope_theta, ids.device)
+        cos, sin = self._rope[T]
+        h = F.embedding(ids, self.embed)
+        for layer in self.layers:
+            h = layer(h, cos, sin)
+        h = rms_norm(h, self.norm, a.eps)
+        logits = self.lm_head(h[:, :-1])                     # (B, T-1, V_local)
+        target = ids[:, 1:]
+        return self._sharded_ce(logits, target)
+
+    def _sharded_ce(self, logits, target):
+        """Mean cross-entropy over column-sharded logits (no gather of the vocabulary)."""
+        lo, hi = self.lm_head.lo, self.lm_head.hi
+        lmax = logits.max(dim=-1).values
+        if self.world > 1:
+            dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
+        sexp = torch.exp(logits - lmax[..., None]).sum(-1)
+        local = (target >= lo) & (target < hi)
+        idx = (target - lo).clamp(0, hi - lo - 1)
+        tgt = torch.where(local, logits.gather(-1, idx[..., None])[..., 0], torch.zeros_like(lmax))
+        if self.world > 1:
+            dist.all_reduce(sexp, group=self.group)
+            dist.all_reduce(tgt, group=self.group)
+        return (torch.log(sexp) + lmax - tgt).mean()

@@ -424,7 +424,7 @@ def tie_bound(x: Sliced, w: Sliced, eng: Engine, wlev=None, fp32_slack: bool = T
 
 
 def mvm_float(x: Sliced, w: Sliced, eng: Engine, rng: np.random.Generator,
-              stuck_field=None, write_field=None, noisy=True):
+              stuck_field=None, write_field=None, noisy=True, dtype=np.float64):
     """Float64 restatement of ``_dot_inference`` including the noise models.
 
     Write variation ``G += G*N(0,wv)`` (memmat_tensor.py:175-180) uses
@@ -454,17 +454,17 @@ def mvm_float(x: Sliced, w: Sliced, eng: Engine, rng: np.random.Generator,
     if noisy and any(s > 0 for s in sig):
         lvl = np.clip(np.rint((G - eng.LGS) / QG), 0, eng.g_level - 1).astype(np.int64)
         G = G * np.exp(np.asarray(sig)[lvl] * rng.standard_normal(G.shape))
-    Gs = (G - eng.LGS).reshape(Sw, -1, p, g.cols_p)
+    Gs = (G - eng.LGS).reshape(Sw, -1, p, g.cols_p).astype(dtype)
     A = dac_levels(x, eng).astype(np.float64)
     Mrows, Kp = A.shape[1], A.shape[2]
     Kt = Kp // p
     V = eng.vread * A / (eng.rdac - 1)
     if noisy and eng.vnoise > 0:
         V = V * (1 + rng.standard_normal(V.shape) * eng.vnoise)
-    V = V.reshape(Sx, Mrows, Kt, p).transpose(0, 2, 1, 3)
+    V = V.reshape(Sx, Mrows, Kt, p).transpose(0, 2, 1, 3).astype(dtype)
     adcRef = (eng.HGS - eng.LGS) * eng.vread * p
     Rj = eng.radc_list(Sw)
-    acc = np.zeros((Kt, Mrows, g.cols_p))
+    acc = np.zeros((Kt, Mrows, g.cols_p), dtype)
     for i in range(Sx):
         for j in range(Sw):
             P = np.matmul(V[i], Gs[j])
@@ -489,3 +489,46 @@ def RE(ytest, ypred):
 def ABSE(ytest, ypred):
     """memintelli/pimpy/utils.py:32-33."""
     return np.sum(np.abs((ytest - ypred) / ytest)) / (ytest.shape[0] * ytest.shape[1])
+
+
+def mvm_float_torch(x: Sliced, w: Sliced, eng: Engine, seed: int = 0, noisy: bool = True):
+    """torch-CPU restatement of ``_dot_inference`` (memmat_tensor.py:260-409) for CPU timing.
+
+    Same arithmetic as ``mvm_float`` in fp32 with torch's multi-threaded CPU
+    kernels (one batched contraction per slice pair, ADC, shift-add, block
+    rescale, K-tile sum), i.e. the structure and speed class of the
+    reference's own CPU path.  Read variation is drawn from a seeded torch
+    generator; stuck-at and write variation are not modelled here.
+    """
+    import torch
+    gen = torch.Generator().manual_seed(seed)
+    p = x.geom.p1
+    Sx, Sw = len(x.slice_method), len(w.slice_method)
+    _, _, mx, cx = slice_tables(x.slice_method)
+    _, _, mw, cw = slice_tables(w.slice_method)
+    g = w.geom
+    QG = (eng.HGS - eng.LGS) / (eng.g_level - 1)
+    Rj = eng.radc_list(Sw)
+    adcRef = (eng.HGS - eng.LGS) * eng.vread * p
+    Kt = x.geom.cols_p // p
+    G = torch.stack([torch.from_numpy(level_map(w.codes(t)[0], mw[t], eng.g_level - 1)) for t in range(Sw)])
+    G = G.float() * QG + eng.LGS                                              # (Sw, Kp, Np)
+    sig = eng.read_sigma()
+    if noisy and sig[0] > 0:
+        G = G * torch.exp(torch.randn(G.shape, generator=gen) * sig[0])
+    Gs = (G - eng.LGS).reshape(Sw, Kt, p, g.cols_p)
+    out = None
+    for i in range(Sx):
+        A = torch.from_numpy(level_map(x.codes(i), mx[i], eng.rdac - 1).reshape(-1, Kt, p)).float()
+        V = (eng.vread * A / (eng.rdac - 1)).transpose(0, 1)                   # (Kt, M, p)
+        if noisy and eng.vnoise > 0:
+            V = V * (1 + torch.randn(V.shape, generator=gen) * eng.vnoise)
+        for j in range(Sw):
+            P = torch.bmm(V, Gs[j])                                           # (Kt, M, Np)
+            P = torch.round(P / adcRef * (Rj[j] - 1)) / (Rj[j] - 1)
+            P = P * float(mx[i] * mw[j] * p * cx[i] * cw[j])
+            out = P if out is None else out.add_(P)
+    sx = torch.from_numpy(np.repeat(x.tile_scale().reshape(-1, Kt), x.geom.p0, axis=0)).float()
+    sw = torch.from_numpy(np.repeat(w.tile_scale()[0], w.geom.p1, axis=1)).float()
+    y = (out * sx.T[:, :, None] * sw[:, None, :]).sum(0)
+    return _crop(y.double().numpy(), x, w)

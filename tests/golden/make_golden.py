@@ -186,6 +186,61 @@ def pack_codes(sliced, slice_method):
     return packed.numpy().astype(np.uint8 if off <= 8 else np.int16)
 
 
+# Layer cases: the reference's own LinearMem / Conv2dMem, noise-free engine, fixed torch seed for init.
+LAYER_CASES = {
+    "conv_bfp_pad": dict(kind="conv", seed=21, x=(2, 3, 10, 10), cin=3, cout=8, k=3, stride=1, padding=1, bias=True,
+                         bw_e=8, sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 64), wp=(32, 32),
+                         wq=(64, 64), eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=1024), inference=True),
+    "conv_s2_int": dict(kind="conv", seed=22, x=(3, 16, 9, 9), cin=16, cout=40, k=3, stride=2, padding=0, bias=False,
+                        bw_e=None, sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 128), wp=(32, 32),
+                        wq=(128, 128), eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=True),
+    "conv_train": dict(kind="conv", seed=23, x=(2, 4, 7, 7), cin=4, cout=6, k=3, stride=1, padding=1, bias=True,
+                       bw_e=None, sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 32), wp=(32, 32),
+                       wq=(32, 32), eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=False),
+    "linear_bias_3d": dict(kind="linear", seed=24, x=(2, 17, 96), cin=96, cout=70, bias=True, bw_e=None,
+                           sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 32), wp=(32, 32), wq=(32, 32),
+                           eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=True),
+    "linear_train": dict(kind="linear", seed=25, x=(33, 100), cin=100, cout=20, bias=True, bw_e=8,
+                         sx=[1, 1, 2, 2, 2], sw=[1, 1, 2, 2, 2], xp=(1, 32), xq=(1, 64), wp=(32, 32), wq=(64, 64),
+                         eng=dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096), inference=False),
+}
+
+
+def run_layer_case(name, spec, DPETensor, LinearMem, Conv2dMem):
+    eng_kw = dict(NOISE_FREE)
+    eng_kw.update(spec["eng"])
+    eng = DPETensor(device=torch.device("cpu"), **eng_kw)
+    torch.manual_seed(spec["seed"])
+    if spec["kind"] == "conv":
+        layer = Conv2dMem(eng, spec["cin"], spec["cout"], spec["k"], spec["sx"], spec["sw"], stride=spec["stride"],
+                          padding=spec["padding"], bias=spec["bias"], device=torch.device("cpu"), bw_e=spec["bw_e"],
+                          input_paral_size=spec["xp"], weight_paral_size=spec["wp"], input_quant_gran=spec["xq"],
+                          weight_quant_gran=spec["wq"])
+    else:
+        layer = LinearMem(eng, spec["cin"], spec["cout"], spec["sx"], spec["sw"], bias=spec["bias"],
+                          device=torch.device("cpu"), bw_e=spec["bw_e"], input_paral_size=spec["xp"],
+                          weight_paral_size=spec["wp"], input_quant_gran=spec["xq"], weight_quant_gran=spec["wq"])
+    x = torch.randn(*spec["x"])
+    if spec["inference"]:
+        layer.inference_mode = True
+        layer.weight_sliced.inference = True
+        with torch.no_grad():
+            y = layer(x)
+        out = {"y": y.numpy()}
+    else:
+        xg = x.clone().requires_grad_(True)
+        y = layer(xg)
+        y.backward(torch.ones_like(y))
+        out = {"y": y.detach().numpy(), "grad_x": xg.grad.numpy(), "grad_w": layer.weight.grad.numpy()}
+        if layer.bias is not None:
+            out["grad_b"] = layer.bias.grad.numpy()
+    out["x"] = x.numpy()
+    out["weight"] = layer.weight.detach().numpy()
+    if layer.bias is not None:
+        out["bias"] = layer.bias.detach().numpy()
+    return out
+
+
 def noise_stats(n_seeds, DPETensor, SlicedData):
     """Per-seed SNR and error moments of the reference's noisy path (config 0 engine)."""
     res = {}
@@ -244,6 +299,14 @@ def main():
             arrays[f"{name}/{k}"] = v
         meta[name] = {k: v for k, v in spec.items()}
         print(f"{name}: y {out['y'].shape} in {time.time() - t0:.2f}s")
+    from memintelli.NN_layers.linear import LinearMem
+    from memintelli.NN_layers.convolution import Conv2dMem
+    for name, spec in LAYER_CASES.items():
+        out = run_layer_case(name, spec, DPETensor, LinearMem, Conv2dMem)
+        for k, v in out.items():
+            arrays[f"{name}/{k}"] = v
+        meta[name] = dict(spec)
+        print(f"{name}: y {out['y'].shape}")
     np.savez_compressed(os.path.join(here, "cases.npz"), **arrays)
     with open(os.path.join(here, "cases.json"), "w") as f:
         json.dump(meta, f, indent=1)

@@ -22,7 +22,22 @@ def load():
 
 
 def names():
-    return list(load()[1].keys())
+    """Matmul (SlicedData x SlicedData) cases."""
+    return [k for k, v in load()[1].items() if "xs" in v]
+
+
+def layer_names():
+    """LinearMem / Conv2dMem cases."""
+    return [k for k, v in load()[1].items() if "kind" in v]
+
+
+def layer_case(name):
+    arrs, meta = load()
+    spec = meta[name]
+    g = {k.split("/", 1)[1]: v for k, v in arrs.items() if k.startswith(name + "/")}
+    eng = dict(NOISE_FREE)
+    eng.update(spec["eng"])
+    return dict(spec=spec, eng=eng, golden=g)
 
 
 NOISE_FREE = dict(write_variation=0.0, read_variation=0.0, vnoise=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0)

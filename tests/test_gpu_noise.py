@@ -1,0 +1,63 @@
+"""Statistical parity of the noisy CIM path (config-0 device model) with the reference (needs a B200).
+
+The reference's per-seed SNR and error moments (256 seeds, paired inputs,
+fixed-seed stuck-at mask) are in tests/golden/noise_stats.json.  The same
+inputs are run here; the stuck-at mask is drawn on the CPU like the reference's.
+"""
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as G
+
+pytestmark = pytest.mark.gpu
+
+SEEDS = 256
+
+
+def _engine(M, cuda, noisy):
+    e = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.0,
+                    rate_stuck_HGS=0.001, rate_stuck_LGS=0.0, read_variation=0.05 if noisy else 0.0,
+                    vnoise=0.05 if noisy else 0.0)
+    e.fault_field_device = "cpu"
+    return e
+
+
+@pytest.mark.parametrize("mode", ["int", "fp"])
+def test_noise_statistics(mode, cuda):
+    import memintelli_flash_b200 as M
+    ref = np.array(G.noise_stats()[mode])
+    bw_e = 8 if mode == "fp" else None
+    en, e0 = _engine(M, cuda, True), _engine(M, cuda, False)
+    sm = torch.tensor([1, 1, 2, 2, 2])
+    rows = []
+    for s in range(SEEDS):
+        g = torch.Generator().manual_seed(1000 + s)
+        x = torch.randn(400, 500, generator=g)
+        w = torch.randn(500, 600, generator=g)
+        ideal = (x.double() @ w.double()).numpy()
+        outs = []
+        for eng in (en, e0):
+            xs = M.SlicedData(sm, bw_e=bw_e, is_weight=False, paral_size=(1, 32), quant_gran=(1, 128),
+                              device=cuda, inference=True)
+            ws = M.SlicedData(sm, bw_e=bw_e, is_weight=True, paral_size=(32, 32), quant_gran=(128, 128),
+                              device=cuda, inference=True)
+            ws.slice_data_imp(eng, w.to(cuda))
+            xs.slice_data_imp(eng, x.to(cuda))
+            torch.manual_seed(50_000 + s)
+            outs.append(eng(xs, ws).double().cpu().numpy())
+        yn, y0 = outs
+        e = yn - y0
+        snr = 10 * np.log10(np.sum(ideal ** 2) / np.sum((ideal - yn) ** 2))
+        rows.append([s, snr, e.mean(), e.std()])
+    mine = np.array(rows)
+    d = mine[:, 1] - ref[:SEEDS, 1]
+    se = d.std(ddof=1) / np.sqrt(SEEDS)
+    print(f"{mode}: SNR mine {mine[:, 1].mean():.4f} ref {ref[:SEEDS, 1].mean():.4f} "
+          f"paired diff {d.mean():+.4f} +- {se:.4f} dB; err std mine {mine[:, 3].mean():.4f} "
+          f"ref {ref[:SEEDS, 3].mean():.4f}; err mean mine {mine[:, 2].mean():.4f} ref {ref[:SEEDS, 2].mean():.4f}")
+    assert abs(d.mean()) < 0.1
+    assert abs(mine[:, 3].mean() / ref[:SEEDS, 3].mean() - 1) < 0.02
+    # mean error: compare with the spread of the per-seed means
+    spread = np.hypot(mine[:, 2].std(ddof=1), ref[:SEEDS, 2].std(ddof=1)) / np.sqrt(SEEDS)
+    assert abs(mine[:, 2].mean() - ref[:SEEDS, 2].mean()) < max(0.02 * abs(ref[:SEEDS, 2].mean()), 4 * spread)
