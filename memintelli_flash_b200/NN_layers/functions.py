@@ -43,6 +43,13 @@ class Conv2dMemRunc(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
+        """Straight-through gradients of Conv2dMemRunc.backward (functions.py:141-266).
+
+        grad_input: transposed convolution of grad_output with the quantised weight.
+        grad_weight: the reference first folds the quantised input patches back to an
+        image, averaging the overlapping copies of each pixel (functions.py:151-160),
+        then takes the convolution weight gradient against that image.
+        """
         xq, wq, bias = ctx.saved_tensors
         in_shape, w_shape, stride, padding, dilation = ctx.geom
         g = grad_output.reshape(grad_output.shape[0], grad_output.shape[1], -1)    # (N, Cout, L)
@@ -51,8 +58,13 @@ class Conv2dMemRunc(torch.autograd.Function):
             cols = torch.matmul(wq.to(g.dtype), g)                                    # (N, C*kh*kw, L)
             grad_input = F.fold(cols, in_shape[2:], w_shape[2:], dilation=dilation, padding=padding, stride=stride)
         if ctx.needs_input_grad[2]:
-            gw = torch.einsum("ncl,nlk->ck", g, xq.to(g.dtype))
-            grad_weight = gw.reshape(w_shape)
+            fold = dict(kernel_size=tuple(w_shape[2:]), dilation=dilation, padding=padding, stride=stride)
+            ones = torch.ones(in_shape, device=g.device, dtype=g.dtype)
+            count = F.fold(F.unfold(ones, **fold), tuple(in_shape[2:]), **fold)
+            count = torch.where(count == 0, torch.ones_like(count), count)
+            image = F.fold(xq.transpose(1, 2).to(g.dtype), tuple(in_shape[2:]), **fold) / count
+            grad_weight = torch.nn.grad.conv2d_weight(image, tuple(w_shape), grad_output, stride=stride,
+                                                      padding=padding, dilation=dilation)
         if bias is not None and ctx.needs_input_grad[4]:
             grad_bias = grad_output.sum((0, 2, 3))
         return None, grad_input, grad_weight, None, grad_bias

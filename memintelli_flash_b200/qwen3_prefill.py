@@ -158,6 +158,7 @@ class Qwen3CimPrefill(torch.nn.Module):
         if T not in self._rope:
             self._rope[T] = rope_cache(T, a.head_dim, a.rope_theta, ids.device)
         cos, sin = self._rope[T]
+        cos, sin = cos[:, None, :], sin[:, None, :]          # (T, 1, head_dim): broadcast over heads
         h = F.embedding(ids, self.embed)
         for layer in self.layers:
             h = layer(h, cos, sin)

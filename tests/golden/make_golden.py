@@ -241,6 +241,18 @@ def run_layer_case(name, spec, DPETensor, LinearMem, Conv2dMem):
     return out
 
 
+def exact_nf(x, w, bw_e):
+    """Exact noise-free restatement (oracle) of the config-0 matmul with the fixed stuck-at mask."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    from oracle import cim_oracle as O
+    xs = O.slice_matrix(x.numpy(), [1, 1, 2, 2, 2], bw_e, (1, 32), (1, 128))
+    ws = O.slice_matrix(w.numpy(), [1, 1, 2, 2, 2], bw_e, (32, 32), (128, 128))
+    eng = O.Engine(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, rate_stuck_HGS=0.001)
+    g = torch.Generator().manual_seed(123)
+    stuck = torch.rand((16, 20, 5, 32, 32), generator=g).numpy()
+    return O.mvm_exact(xs, ws, eng, O.weight_levels(ws, eng, stuck))
+
+
 def noise_stats(n_seeds, DPETensor, SlicedData):
     """Per-seed SNR and error moments of the reference's noisy path (config 0 engine)."""
     res = {}
@@ -270,7 +282,10 @@ def noise_stats(n_seeds, DPETensor, SlicedData):
             yn, y0 = outs
             e = yn - y0
             snr = 10 * np.log10(np.sum(ideal ** 2) / np.sum((ideal - yn) ** 2))
-            rows.append([s, snr, float(e.mean()), float(e.std()), float(np.sqrt(np.mean(y0 ** 2)))])
+            # the reference's own noise-free output carries its fp32 tie-rounding bias; record it
+            # against the exact restatement so means can be compared on one baseline
+            tie_bias = float((y0 - exact_nf(x, w, bw_e)).mean())
+            rows.append([s, snr, float(e.mean()), float(e.std()), float(np.sqrt(np.mean(y0 ** 2))), tie_bias])
         res[key] = rows
         print(f"noise stats {key}: {n_seeds} seeds in {time.time() - t0:.1f}s; "
               f"SNR {np.mean([r[1] for r in rows]):.3f} +- {np.std([r[1] for r in rows]):.3f}")
@@ -313,7 +328,7 @@ def main():
     if not args.skip_stats:
         st = noise_stats(args.seeds, DPETensor, SlicedData)
         with open(os.path.join(here, "noise_stats.json"), "w") as f:
-            json.dump({"columns": ["seed", "snr_db", "err_mean", "err_std", "y_rms"], **st}, f)
+            json.dump({"columns": ["seed", "snr_db", "err_mean", "err_std", "y_rms", "tie_bias"], **st}, f)
 
 
 if __name__ == "__main__":

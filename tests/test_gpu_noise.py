@@ -58,6 +58,9 @@ def test_noise_statistics(mode, cuda):
           f"ref {ref[:SEEDS, 3].mean():.4f}; err mean mine {mine[:, 2].mean():.4f} ref {ref[:SEEDS, 2].mean():.4f}")
     assert abs(d.mean()) < 0.1
     assert abs(mine[:, 3].mean() / ref[:SEEDS, 3].mean() - 1) < 0.02
-    # mean error: compare with the spread of the per-seed means
-    spread = np.hypot(mine[:, 2].std(ddof=1), ref[:SEEDS, 2].std(ddof=1)) / np.sqrt(SEEDS)
-    assert abs(mine[:, 2].mean() - ref[:SEEDS, 2].mean()) < max(0.02 * abs(ref[:SEEDS, 2].mean()), 4 * spread)
+    # mean error against the exact noise-free result: the reference's own noise-free output carries
+    # its fp32 tie-rounding bias (column 5), ours is exact to fp32, so compare on the exact baseline
+    ref_mean = ref[:SEEDS, 2] + ref[:SEEDS, 5]
+    spread = np.hypot(mine[:, 2].std(ddof=1), ref_mean.std(ddof=1)) / np.sqrt(SEEDS)
+    print(f"{mode}: err mean vs exact mine {mine[:, 2].mean():.4f} ref {ref_mean.mean():.4f} +- {spread:.4f}")
+    assert abs(mine[:, 2].mean() - ref_mean.mean()) < max(0.02 * abs(ref_mean.mean()), 4 * spread)

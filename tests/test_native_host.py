@@ -1,0 +1,111 @@
+"""The C-ABI library: loads, exports every declared symbol, and its host-only logic (no GPU)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from memintelli_flash_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _declared():
+    with open(os.path.join(ROOT, "include", "memintelli_b200.h")) as f:
+        src = f.read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*|uint64_t)\s+(mib_\w+)\s*\(", src, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    L = N.lib()
+    names = _declared()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(L, n), n
+    assert set(names) == set(N.EXPORTS)
+    assert b"sm_100a" in L.mib_version()
+
+
+def _spec(sm, paral, qg, bfp=0):
+    s = N.SliceSpec()
+    s.n_slices = len(sm)
+    for i, v in enumerate(sm):
+        s.slice_method[i] = v
+    s.bfp = bfp
+    s.paral[0], s.paral[1] = paral
+    s.quant_gran[0], s.quant_gran[1] = qg
+    return s
+
+
+def _dev(radc, rdac=4, g=4, sigma=0.0):
+    d = N.DeviceSpec()
+    d.hgs, d.lgs, d.g_level, d.rdac = 1e-5, 1e-8, g, rdac
+    if isinstance(radc, list):
+        d.n_radc = len(radc)
+        for i, v in enumerate(radc):
+            d.radc[i] = v
+    else:
+        d.n_radc, d.radc[0] = 1, radc
+    d.n_read_sigma, d.read_sigma[0] = 1, sigma
+    return d
+
+
+def _kg(k, p=32, qg=128):
+    kg = N.KGeom()
+    kg.k, kg.p, kg.pp = k, p, max(32, p)
+    kg.kp = -(-k // qg) * qg
+    kg.kt = kg.kp // p
+    return kg
+
+
+def _plan(xs, ws, kg, dev):
+    mode, n = N.c_i32(0), N.c_i32(0)
+    rc = N.lib().mib_adc_plan(xs, ws, kg, dev, mode, n, None)
+    return rc, mode.value, n.value
+
+
+SM = [1, 1, 2, 2, 2]
+
+
+def test_adc_plan_dyadic_uses_magic_rounding():
+    rc, mode, n = _plan(_spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 32), (128, 128)), _kg(500), _dev(4096))
+    assert rc == 0 and mode == 0 and n == 0
+
+
+def test_adc_plan_non_dyadic_needs_table():
+    xs, ws, kg, dev = _spec(SM, (1, 32), (1, 64)), _spec(SM, (32, 32), (64, 64)), _kg(100, qg=64), _dev(1024)
+    rc, mode, n = _plan(xs, ws, kg, dev)
+    assert rc == 0 and mode & N.MODE_LUT and n == 5 * 289
+    table = (N.c_i32 * n)()
+    mode_c, n_c = N.c_i32(0), N.c_i32(0)
+    assert N.lib().mib_adc_plan(xs, ws, kg, dev, mode_c, n_c, table) == 0
+    # round_half_even(S * 1023 / 288) for every reachable S of one slice
+    assert list(table)[:289] == [round(s * 1023 / 288) for s in range(289)]
+
+
+def test_adc_plan_noisy_skips_table():
+    rc, mode, n = _plan(_spec(SM, (1, 32), (1, 64)), _spec(SM, (32, 32), (64, 64)), _kg(100, qg=64),
+                        _dev(1024, sigma=0.05))
+    assert rc == 0 and n == 0
+
+
+def test_adc_plan_radc_list_length_checked():
+    rc, _, _ = _plan(_spec([1, 1, 2, 2], (32, 32), (64, 64)), _spec([1, 1, 2, 2], (32, 32), (64, 64)),
+                     _kg(100, qg=64), _dev([4096, 2048, 1024]))
+    assert rc == N.MIB_ERR_PARAM
+    assert b"must match number of weight slices" in N.lib().mib_last_error()
+
+
+def test_slice_method_first_bit_checked():
+    rc, _, _ = _plan(_spec([2, 2, 2], (1, 32), (1, 64)), _spec(SM, (32, 32), (64, 64)), _kg(100, qg=64), _dev(4096))
+    assert rc == N.MIB_ERR_PARAM
+    assert b"first bit" in N.lib().mib_last_error()
+    with pytest.raises(ValueError):
+        N.check(rc)
+
+
+def test_mvm_rejects_bad_arguments_before_any_device_work():
+    xs, ws = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 64), (128, 128))
+    rc = N.lib().mib_mvm(None, None, 10, xs, None, None, 10, ws, _kg(128), _dev(4096), 0, None, 0, None, None,
+                         None, None, None)
+    assert rc == N.MIB_ERR_PARAM

@@ -1,0 +1,67 @@
+"""The CPU oracle against the reference's golden vectors (no GPU)."""
+import numpy as np
+import pytest
+
+import golden_cases as G
+from helpers import oracle_pair, rel_norm
+from oracle import cim_oracle as O
+
+
+@pytest.mark.parametrize("name", G.names())
+def test_codes_match_reference(name):
+    c = G.case(name)
+    s, g = c["spec"], c["golden"]
+    xs, ws, _, _ = oracle_pair(c)
+    assert np.array_equal(G.packed_to_rows(g["x_packed"], len(s["xs"]) == 3), xs.q)
+    assert np.array_equal(G.packed_to_rows(g["w_packed"], False)[0], ws.q[0])
+    tile_max_x = np.repeat(np.repeat(xs.bmax, xs.geom.qg0 // xs.geom.p0, 1), xs.geom.qg1 // xs.geom.p1, 2)
+    gx = g["x_max"][..., 0, 0]
+    assert np.array_equal(tile_max_x[0] if xs.squeeze else tile_max_x, gx)
+    if s["bw_e"]:
+        ex = np.repeat(np.repeat(xs.ebias, xs.geom.qg0 // xs.geom.p0, 1), xs.geom.qg1 // xs.geom.p1, 2)
+        assert np.array_equal(ex[0] if xs.squeeze else ex, g["x_ebias"][..., 0, 0])
+    if "x_quantized" in g:
+        assert np.array_equal(xs.deq if not xs.squeeze else xs.deq[0], g["x_quantized"])
+
+
+@pytest.mark.parametrize("name", [n for n in G.names() if n != "write_var"])
+def test_exact_within_tie_bound_of_reference(name):
+    c = G.case(name)
+    xs, ws, eng, wl = oracle_pair(c)
+    y = O.mvm_exact(xs, ws, eng, wl)
+    y_ref = c["golden"]["y"].astype(np.float64)
+    b = O.tie_bound(xs, ws, eng, wl)
+    assert np.all(np.abs(y - y_ref) <= b + 1e-5 * np.abs(y_ref).max())
+    if name.startswith("tiefree") or name in ("percol_2slice",):
+        assert rel_norm(y, y_ref) < 1e-5
+
+
+def test_write_variation_restatement():
+    c = G.case("write_var")
+    xs, ws, eng, _ = oracle_pair(c)
+    y = O.mvm_float(xs, ws, eng, np.random.default_rng(0), c["fields"].get("stuck"), c["fields"]["write"],
+                    noisy=False)
+    assert rel_norm(y, c["golden"]["y"]) < 1e-3
+
+
+def test_adc_round_half_even():
+    S = np.arange(0, 289)
+    q = O.adc_round(S, 4095, 288)
+    exact = np.array([round(s * 4095 / 288) for s in S])        # Python round is half-even
+    assert np.array_equal(q, exact)
+    assert O.adc_ties(np.array([16, 48, 17]), 4095, 288).tolist() == [True, True, False]
+
+
+def test_bfp_exponent_edges():
+    # torch's fp32 floor(log2(.)) rounds log2 to fp32 first: just below 2^-14 it gives -14, not -15
+    v = np.float32(6.1035153e-05)
+    assert O.bfp_exponent(np.array([v]))[0] == -14
+    assert O.bfp_exponent(np.array([np.float32(0.0)]))[0] == -34
+
+
+def test_noise_stats_fixture_shape():
+    st = G.noise_stats()
+    for k in ("int", "fp"):
+        a = np.array(st[k])
+        assert a.shape[0] >= 128 and a.shape[1] == 6
+        assert 5 < a[:, 1].mean() < 20
