@@ -65,7 +65,6 @@ enum MvmMode : int {
 };
 
 constexpr int kMvmBM = 128;
-constexpr int kMvmBN = 128;
 constexpr int kMaxLut = 4096;
 
 struct MvmArgs {
@@ -100,6 +99,7 @@ cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, int6
 void launch_block_exp(const float* bmax, float* bexp, int64_t n, cudaStream_t stream);
 void count_launch(int n = 1);
 size_t mvm_smem_bytes(const MvmArgs& a);
+int mvm_column_groups(int sy);   // output tile width BN = 16 * mvm_column_groups(Sy)
 cudaError_t launch_mvm(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, int kind, int acc_mode,
                        cudaStream_t stream);
 

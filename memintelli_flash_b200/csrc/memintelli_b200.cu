@@ -141,15 +141,17 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
-// 3-D map over operand planes [S][rows][kt*pp]; box = one crossbar tile of 128 rows, all slices.
-int encode_planes(CUtensorMap* map, const void* base, int kind, int64_t rows, int64_t row_elems, int slices, int pp) {
+// 3-D map over operand planes [S][rows][kt*pp]; box = one crossbar tile of `box_rows` rows, all slices.
+int encode_planes(CUtensorMap* map, const void* base, int kind, int64_t rows, int64_t row_elems, int slices, int pp,
+                  int box_rows) {
   auto enc = tensor_map_encoder();
   if (!enc) return fail(MIB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
   const int es = esize(kind);
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(row_elems), static_cast<cuuint64_t>(rows),
                               static_cast<cuuint64_t>(slices)};
   const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_elems * es), static_cast<cuuint64_t>(rows * row_elems * es)};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(pp), 128u, static_cast<cuuint32_t>(slices)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(pp), static_cast<cuuint32_t>(box_rows),
+                             static_cast<cuuint32_t>(slices)};
   const cuuint32_t estr[3] = {1, 1, 1};
   const int rb = pp * es;
   const CUtensorMapSwizzle swz = rb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
@@ -492,14 +494,15 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   a.Sx = tx.S;
   a.Sy = tw.S;
   a.row_bytes = kg->pp * esize(operand_kind);
+  const int bn = 16 * mib::mvm_column_groups(tw.S);
   a.a_slice_bytes = static_cast<uint32_t>(mib::kMvmBM * a.row_bytes);
-  a.b_slice_bytes = static_cast<uint32_t>(mib::kMvmBN * a.row_bytes);
+  a.b_slice_bytes = static_cast<uint32_t>(bn * a.row_bytes);
   a.stage_bytes = static_cast<uint32_t>(tx.S) * a.a_slice_bytes + static_cast<uint32_t>(tw.S) * a.b_slice_bytes;
   a.lut_len = pl.lut_len;
   a.lut = adc_table;
   a.lut_smem = (pl.mode & mib::MODE_LUT) && static_cast<size_t>(tw.S) * pl.lut_len * 4 <= 48 * 1024 ? 1 : 0;
   const size_t budget = 225 * 1024;
-  const size_t fixed = 1024 + sizeof(float) * mib::kMvmBM * mib::kMvmBN + sizeof(mib::SmemCtl) + (a.lut_smem ? static_cast<size_t>(tw.S) * pl.lut_len * 4 : 0);
+  const size_t fixed = 1024 + sizeof(mib::SmemCtl) + (a.lut_smem ? static_cast<size_t>(tw.S) * pl.lut_len * 4 : 0);
   if (fixed + a.stage_bytes > budget) return fail(MIB_ERR_UNSUPPORTED, "one K tile of all slices exceeds shared memory");
   a.stages = static_cast<int32_t>(std::min<size_t>(8, (budget - fixed) / a.stage_bytes));
   a.flush_tiles = pl.flush;
@@ -524,8 +527,8 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   a.bias = bias;
   a.acc_dump = acc_dump;
   CUtensorMap ta, tb;
-  if (int r = encode_planes(&ta, a_planes, operand_kind, m, kg->kt * kg->pp, tx.S, kg->pp)) return r;
-  if (int r = encode_planes(&tb, b_planes, operand_kind, n, kg->kt * kg->pp, tw.S, kg->pp)) return r;
+  if (int r = encode_planes(&ta, a_planes, operand_kind, m, kg->kt * kg->pp, tx.S, kg->pp, mib::kMvmBM)) return r;
+  if (int r = encode_planes(&tb, b_planes, operand_kind, n, kg->kt * kg->pp, tw.S, kg->pp, bn)) return r;
   cudaError_t e = mib::launch_mvm(ta, tb, a, operand_kind, mode, stream);
   if (e != cudaSuccess) return cuda_fail(e, "mvm launch");
   return MIB_OK;

@@ -1,18 +1,23 @@
 // Fused crossbar MVM on tcgen05 tensor cores.
 //
-// Computes, for one 128x128 output tile per CTA,
+// For one 128 x BN output tile per CTA it computes
 //   y[r,n] = sum_t  xs[t,r] * ws[t,n] * sum_{i,j} ADC_j( S_ij[r,t,n] ) * w_ij
 // with S_ij[r,t,n] = sum_{k in tile t} A_i[r,k] * L_j[k,n] (exact crossbar sum),
 // ADC_j(S) = round_half_even(S * (radc_j - 1) / D) and w_ij = m_i m_j c_i c_j * p/(radc-1),
-// i.e. DPETensor._dot_inference (memmat_tensor.py:260-409) without ever writing
-// the per slice-pair partial tensor to HBM.
+// i.e. DPETensor._dot_inference (memmat_tensor.py:260-409), without writing the
+// per slice-pair partial tensor anywhere.
 //
-// Warp roles (320 threads, one CTA per SM):
-//   warps 0-7  epilogue: tcgen05.ld of each slice-pair accumulator, ADC,
-//              shift-add, per-tile rescale, output store
-//   warp 8     TMA producer (all slices of A and B for one K tile per stage)
-//   warp 9     MMA issuer: one tcgen05.mma chain per (K tile, slice pair) into
-//              one of 4 TMEM slots of 128 fp32 columns
+// One tcgen05.mma chain per (K tile t, input slice i) covers every weight slice j
+// at once: the Sy weight-slice tiles of a stage sit back to back in shared
+// memory, so B is one K-major operand of Sy*BN rows and the accumulator is a
+// 128 x (Sy*BN) fp32 block of tensor memory.  Two such slots alternate.
+//
+// Warp roles (one CTA per SM):
+//   warps 0 .. 4*CG-1  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
+//                      columns 16*(w/4).. of every weight slice; ADC, shift-add,
+//                      per-tile rescale, output store
+//   warp 4*CG          TMA producer (all slices of A and B for one K tile per stage)
+//   warp 4*CG+1        MMA issuer
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -20,12 +25,9 @@ namespace mib {
 
 namespace {
 
-constexpr int kEpiWarps = 8;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
-constexpr int kThreads = 320;
-constexpr int kSlots = 4;
+constexpr int kSlots = 2;
 constexpr int kTmemCols = 512;
+constexpr int kSlotCols = 256;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer (half-even)
 constexpr uint32_t kMagicBits = 0x4B400000u;
 
@@ -44,27 +46,50 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
-template <int KIND, int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+// 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__host__ __device__ constexpr int column_groups(int sy) { return 16 / sy > 4 ? 4 : (16 / sy < 2 ? 2 : 16 / sy); }
+
+#ifndef MIB_USE_FFMA2
+#define MIB_USE_FFMA2 1
+#endif
+
+template <int KIND, int MODE, int SY>
+__global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     mvm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const __grid_constant__ MvmArgs P) {
+  constexpr int CG = column_groups(SY);
   constexpr bool kLut = (MODE & MODE_LUT) != 0;
   constexpr bool kFloatAcc = (MODE & MODE_FLOATACC) != 0;
   constexpr bool kDump = (MODE & MODE_DUMP) != 0;
+  constexpr int kEpiWarps = 4 * CG;
+  constexpr int kProducerWarp = kEpiWarps;
+  constexpr int kMmaWarp = kEpiWarps + 1;
+  constexpr int BN = 16 * CG;
+  constexpr int kJChunk = CG >= 4 ? 2 : SY;   // weight slices loaded from TMEM per wait (register budget)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // [stages x stage_bytes] operand ring | [128 cols][128 rows] fp32 output tile | control | code table
-  float* out_s = reinterpret_cast<float*>(smem + static_cast<size_t>(P.stages) * P.stage_bytes);
-  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(out_s + kMvmBM * kMvmBN);
+  SmemCtl* ctl = reinterpret_cast<SmemCtl*>(smem + static_cast<size_t>(P.stages) * P.stage_bytes);
   int32_t* lut_s = reinterpret_cast<int32_t*>(ctl + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kMvmBM;
-  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kMvmBN;
+  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+  constexpr int Sy = SY;
+  const int Sx = P.Sx, Kt = static_cast<int>(P.Kt), stages = P.stages;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < P.stages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&ctl->full[s], 1);
       mbar_init(&ctl->empty[s], 1);
     }
@@ -78,7 +103,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if constexpr (kLut) {
     if (P.lut_smem)
-      for (int i = threadIdx.x; i < P.Sy * P.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
+      for (int i = threadIdx.x; i < Sy * P.lut_len; i += blockDim.x) lut_s[i] = P.lut[i];
   }
   if (warp == kProducerWarp) {
     tmem_alloc(&ctl->tmem_base, kTmemCols);
@@ -95,58 +120,67 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tma_a);
       tma_prefetch_desc(&tma_b);
-      int64_t issued = 0;
-      for (int64_t t = 0; t < P.Kt; ++t) {
-        const int s = static_cast<int>(t % P.stages);
-        const uint32_t use = static_cast<uint32_t>(t / P.stages);
-        if (t >= P.stages && !mbar_wait(&ctl->empty[s], (use - 1) & 1, abort, 11)) break;
+      int issued = 0;
+      int s = 0;
+      uint32_t phase = 0;
+      for (int t = 0; t < Kt; ++t) {
+        if (t >= stages && !mbar_wait(&ctl->empty[s], phase ^ 1u, abort, 11)) break;
         uint8_t* a_dst = smem + static_cast<size_t>(s) * P.stage_bytes;
-        uint8_t* b_dst = a_dst + static_cast<size_t>(P.Sx) * P.a_slice_bytes;
+        uint8_t* b_dst = a_dst + static_cast<size_t>(Sx) * P.a_slice_bytes;
         mbar_arrive_expect_tx(&ctl->full[s], P.stage_bytes);
-        tma_load_3d(a_dst, &tma_a, &ctl->full[s], static_cast<int>(t * P.pp), static_cast<int>(m0), 0);
-        tma_load_3d(b_dst, &tma_b, &ctl->full[s], static_cast<int>(t * P.pp), static_cast<int>(n0), 0);
+        tma_load_3d(a_dst, &tma_a, &ctl->full[s], t * P.pp, static_cast<int>(m0), 0);
+        tma_load_3d(b_dst, &tma_b, &ctl->full[s], t * P.pp, static_cast<int>(n0), 0);
         issued = t + 1;
+        if (++s == stages) {
+          s = 0;
+          phase ^= 1u;
+        }
       }
       // no TMA write may still be in flight when the CTA exits
-      const int64_t first = issued > P.stages ? issued - P.stages : 0;
-      for (int64_t t = first; t < issued; ++t)
-        mbar_wait_drain(&ctl->full[t % P.stages], static_cast<uint32_t>(t / P.stages) & 1, 12);
+      const int first = issued > stages ? issued - stages : 0;
+      for (int t = first; t < issued; ++t)
+        mbar_wait_drain(&ctl->full[t % stages], static_cast<uint32_t>(t / stages) & 1u, 12);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA
     if (lane == 0) {
-      const uint32_t idesc = instr_desc_m128(kMvmBN);
+      const uint32_t idesc = instr_desc_m128(static_cast<uint32_t>(Sy * BN));
       const int ksteps = P.row_bytes / 32;
-      int64_t g = 0;
+      int slot = 0, s = 0, uses = 0;
+      uint32_t sphase = 0, tphase = 0;
       bool ok = true;
-      for (int64_t t = 0; t < P.Kt && ok; ++t) {
-        const int s = static_cast<int>(t % P.stages);
-        if (!mbar_wait(&ctl->full[s], static_cast<uint32_t>(t / P.stages) & 1, abort, 21)) {
+      for (int t = 0; t < Kt && ok; ++t) {
+        if (!mbar_wait(&ctl->full[s], sphase, abort, 21)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t a_base = smem_u32(smem + static_cast<size_t>(s) * P.stage_bytes);
-        const uint32_t b_base = a_base + P.Sx * P.a_slice_bytes;
-        for (int i = 0; i < P.Sx && ok; ++i) {
-          for (int j = 0; j < P.Sy; ++j, ++g) {
-            const int slot = static_cast<int>(g % kSlots);
-            if (g >= kSlots &&
-                !mbar_wait(&ctl->tempty[slot], static_cast<uint32_t>(g / kSlots - 1) & 1, abort, 22)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t d = tmem_base + slot * kMvmBN;
-            for (int kk = 0; kk < ksteps; ++kk) {
-              const uint64_t ad = smem_desc(a_base + i * P.a_slice_bytes + kk * 32, P.row_bytes);
-              const uint64_t bd = smem_desc(b_base + j * P.b_slice_bytes + kk * 32, P.row_bytes);
-              tc_mma<KIND>(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
-            }
-            tc_commit(&ctl->tfull[slot]);
+        const uint32_t b_base = a_base + Sx * P.a_slice_bytes;
+        for (int i = 0; i < Sx; ++i) {
+          if (uses >= kSlots && !mbar_wait(&ctl->tempty[slot], tphase ^ 1u, abort, 22)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem_base + slot * kSlotCols;
+          for (int kk = 0; kk < ksteps; ++kk) {
+            const uint64_t ad = smem_desc(a_base + i * P.a_slice_bytes + kk * 32, P.row_bytes);
+            const uint64_t bd = smem_desc(b_base + kk * 32, P.row_bytes);
+            tc_mma<KIND>(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(&ctl->tfull[slot]);
+          ++uses;
+          if (++slot == kSlots) {
+            slot = 0;
+            tphase ^= 1u;
           }
         }
         if (ok) tc_commit(&ctl->empty[s]);
+        if (++s == stages) {
+          s = 0;
+          sphase ^= 1u;
+        }
       }
       // every issued MMA has completed before TMEM is released
       tc_commit(&ctl->drain);
@@ -154,84 +188,124 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------- epilogue
-    const int q = warp & 3;           // TMEM lane quarter this warp may access
-    const int cb = (warp >> 2) * 64;  // 64-column half of the tile
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int cg = (warp >> 2) * 16;    // 16-column group inside each weight slice's BN columns
     const int64_t row = m0 + q * 32 + lane;
-    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cb;
-    // output accumulators live in shared memory, column-major, so lanes (rows) hit consecutive words
-    float* out_col = out_s + static_cast<size_t>(cb) * kMvmBM + q * 32 + lane;
-    uint32_t acc[64];
+    const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cg;
+    float cj[8];
 #pragma unroll
-    for (int c = 0; c < 64; ++c) {
+    for (int j = 0; j < 8; ++j) cj[j] = P.cadc[j];
+    uint32_t acc[16];
+    float out[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
       acc[c] = 0u;
-      out_col[c * kMvmBM] = 0.0f;
+      out[c] = 0.0f;
     }
-    int64_t g = 0;
-    int cnt = 0;
+    const int32_t* lut = kLut ? (P.lut_smem ? lut_s : P.lut) : nullptr;
+    int slot = 0, cnt = 0;
+    uint32_t tphase = 0;
     bool ok = true;
-    for (int64_t t = 0; t < P.Kt && ok; ++t) {
-      for (int i = 0; i < P.Sx && ok; ++i) {
-        for (int j = 0; j < P.Sy; ++j, ++g) {
-          const int slot = static_cast<int>(g % kSlots);
-          if (!warp_wait(&ctl->tfull[slot], static_cast<uint32_t>(g / kSlots) & 1, abort, 31)) {
-            ok = false;
-            break;
+    for (int t = 0; t < Kt && ok; ++t) {
+      for (int i = 0; i < Sx; ++i) {
+        if (!warp_wait(&ctl->tfull[slot], tphase, abort, 31)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = lane_addr + slot * kSlotCols;
+        uint32_t wi[SY];
+        float wfi[SY];
+#pragma unroll
+        for (int j = 0; j < SY; ++j) {
+          wi[j] = static_cast<uint32_t>(P.wpair[i * 8 + j]);
+          if constexpr (kFloatAcc) wfi[j] = P.wfpair[i * 8 + j];
+        }
+#pragma unroll
+        for (int j0 = 0; j0 < SY; j0 += kJChunk) {
+          uint32_t r[kJChunk][16];
+#pragma unroll
+          for (int jj = 0; jj < kJChunk; ++jj)
+            if (j0 + jj < SY) tmem_ld16(base + (j0 + jj) * BN, r[jj]);
+          tmem_wait_ld();
+          if (j0 + kJChunk >= SY) {
+            // every column of this slot is in registers: hand the slot back to the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ctl->tempty[slot]);
           }
-          tc_fence_after();
-          const float cj = P.cadc[j];
-          const uint32_t wij = static_cast<uint32_t>(P.wpair[i * 8 + j]);
-          const float wfij = P.wfpair[i * 8 + j];
-          const int32_t* lut_j = (P.lut_smem ? lut_s : P.lut) + j * P.lut_len;
 #pragma unroll
-          for (int ch = 0; ch < 2; ++ch) {
-            uint32_t r[32];
-            tmem_ld32(lane_addr + slot * kMvmBN + ch * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const float sv = __uint_as_float(r[c]);
+          for (int jj = 0; jj < kJChunk; ++jj) {
+            const int j = j0 + jj;
+            if (j < SY) {
               if constexpr (kLut) {
-                const int idx = static_cast<int>(__float_as_uint(sv + kMagic) - kMagicBits);
-                const int32_t code = lut_j[min(max(idx, 0), P.lut_len - 1)];
-                if constexpr (kFloatAcc)
-                  acc[ch * 32 + c] = __float_as_uint(fmaf(static_cast<float>(code), wfij, __uint_as_float(acc[ch * 32 + c])));
-                else
-                  acc[ch * 32 + c] += wij * static_cast<uint32_t>(code);
+                const int32_t* lj = lut + j * P.lut_len;
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                  const int idx = static_cast<int>(__float_as_uint(__uint_as_float(r[jj][c]) + kMagic) - kMagicBits);
+                  const int32_t code = lj[min(max(idx, 0), P.lut_len - 1)];
+                  if constexpr (kFloatAcc)
+                    acc[c] = __float_as_uint(fmaf(static_cast<float>(code), wfi[j], __uint_as_float(acc[c])));
+                  else
+                    acc[c] += wi[j] * static_cast<uint32_t>(code);
+                }
               } else {
-                const float tq = fmaf(sv, cj, kMagic);
-                if constexpr (kFloatAcc)
-                  acc[ch * 32 + c] = __float_as_uint(fmaf(tq - kMagic, wfij, __uint_as_float(acc[ch * 32 + c])));
-                else
-                  acc[ch * 32 + c] += wij * __float_as_uint(tq);
+#if MIB_USE_FFMA2
+                const float2 cc = make_float2(cj[j], cj[j]);
+                const float2 mm = make_float2(kMagic, kMagic);
+#pragma unroll
+                for (int c = 0; c < 16; c += 2) {
+                  const float2 tq =
+                      __ffma2_rn(make_float2(__uint_as_float(r[jj][c]), __uint_as_float(r[jj][c + 1])), cc, mm);
+                  if constexpr (kFloatAcc) {
+                    acc[c] = __float_as_uint(fmaf(tq.x - kMagic, wfi[j], __uint_as_float(acc[c])));
+                    acc[c + 1] = __float_as_uint(fmaf(tq.y - kMagic, wfi[j], __uint_as_float(acc[c + 1])));
+                  } else {
+                    acc[c] += wi[j] * __float_as_uint(tq.x);
+                    acc[c + 1] += wi[j] * __float_as_uint(tq.y);
+                  }
+                }
+#else
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                  const float tq = fmaf(__uint_as_float(r[jj][c]), cj[j], kMagic);
+                  if constexpr (kFloatAcc)
+                    acc[c] = __float_as_uint(fmaf(tq - kMagic, wfi[j], __uint_as_float(acc[c])));
+                  else
+                    acc[c] += wi[j] * __float_as_uint(tq);
+                }
+#endif
               }
             }
           }
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctl->tempty[slot]);
+        }
+        if (++slot == kSlots) {
+          slot = 0;
+          tphase ^= 1u;
         }
       }
       if (!ok) break;
       ++cnt;
-      if (kDump || cnt == P.flush_tiles || t == P.Kt - 1) {
-        const float xsv = row < P.M ? __ldg(P.xs + t * P.M + row) : 0.0f;
+      if (kDump || cnt == P.flush_tiles || t == Kt - 1) {
+        const float xsv = row < P.M ? __ldg(P.xs + static_cast<int64_t>(t) * P.M + row) : 0.0f;
         const float rs = kFloatAcc ? xsv : xsv * P.out_scale;
         const uint32_t off = (kLut || kFloatAcc) ? 0u : static_cast<uint32_t>(cnt) * P.tile_offset;
+        const float* wsr = P.ws + static_cast<int64_t>(t) * P.N + n0 + cg;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const int64_t n = n0 + cb + c;
-          const float wsv = n < P.N ? __ldg(P.ws + t * P.N + n) : 0.0f;
+        for (int c = 0; c < 16; ++c) {
+          const bool in = n0 + cg + c < P.N;
+          const float wsv = in ? __ldg(wsr + c) : 0.0f;
           float v;
           if constexpr (kFloatAcc) {
             v = __uint_as_float(acc[c]);
           } else {
             const int32_t iv = static_cast<int32_t>(acc[c] - off);
             if constexpr (kDump) {
-              if (row < P.M && n < P.N) P.acc_dump[(t * P.M + row) * P.N + n] = iv;
+              if (row < P.M && in) P.acc_dump[(static_cast<int64_t>(t) * P.M + row) * P.N + n0 + cg + c] = iv;
             }
             v = static_cast<float>(iv);
           }
-          out_col[c * kMvmBM] = fmaf(v, rs * wsv, out_col[c * kMvmBM]);
+          out[c] = fmaf(v, rs * wsv, out[c]);
           acc[c] = 0u;
         }
         cnt = 0;
@@ -242,9 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t rr = row - grp * P.rows_per_group;
       float* yb = P.y + grp * P.group_stride + rr * P.row_stride;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const int64_t n = n0 + cb + c;
-        if (n < P.N) yb[n * P.col_stride] = out_col[c * kMvmBM] + (P.bias ? __ldg(P.bias + n) : 0.0f);
+      for (int c = 0; c < 16; ++c) {
+        const int64_t n = n0 + cg + c;
+        if (n < P.N) yb[n * P.col_stride] = out[c] + (P.bias ? __ldg(P.bias + n) : 0.0f);
       }
     }
   }
@@ -256,36 +330,59 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int KIND, int MODE>
+template <int KIND, int MODE, int SY>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, size_t smem,
                        cudaStream_t stream) {
-  auto fn = mvm_kernel<KIND, MODE>;
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
-  dim3 grid(static_cast<unsigned>((a.N + kMvmBN - 1) / kMvmBN), static_cast<unsigned>((a.M + kMvmBM - 1) / kMvmBM));
-  fn<<<grid, kThreads, smem, stream>>>(ta, tb, a);
+  auto fn = mvm_kernel<KIND, MODE, SY>;
+  static bool configured = false;  // per template instance; the smem cap is the same for every call
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  constexpr int CG = column_groups(SY);
+  constexpr int BN = 16 * CG;
+  dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + kMvmBM - 1) / kMvmBM));
+  fn<<<grid, 32 * (4 * CG + 2), smem, stream>>>(ta, tb, a);
   count_launch();
   return cudaGetLastError();
+}
+
+template <int KIND, int SY>
+cudaError_t launch_sy(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, int mode, size_t smem,
+                      cudaStream_t stream) {
+  switch (mode) {
+    case 0: return launch_one<KIND, 0, SY>(ta, tb, a, smem, stream);
+    case MODE_LUT: return launch_one<KIND, MODE_LUT, SY>(ta, tb, a, smem, stream);
+    case MODE_FLOATACC: return launch_one<KIND, MODE_FLOATACC, SY>(ta, tb, a, smem, stream);
+    case MODE_LUT | MODE_FLOATACC: return launch_one<KIND, MODE_LUT | MODE_FLOATACC, SY>(ta, tb, a, smem, stream);
+    case MODE_DUMP: return launch_one<KIND, MODE_DUMP, SY>(ta, tb, a, smem, stream);
+    case MODE_DUMP | MODE_LUT: return launch_one<KIND, MODE_DUMP | MODE_LUT, SY>(ta, tb, a, smem, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 template <int KIND>
 cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, int mode, size_t smem,
                         cudaStream_t stream) {
-  switch (mode) {
-    case 0: return launch_one<KIND, 0>(ta, tb, a, smem, stream);
-    case MODE_LUT: return launch_one<KIND, MODE_LUT>(ta, tb, a, smem, stream);
-    case MODE_FLOATACC: return launch_one<KIND, MODE_FLOATACC>(ta, tb, a, smem, stream);
-    case MODE_LUT | MODE_FLOATACC: return launch_one<KIND, MODE_LUT | MODE_FLOATACC>(ta, tb, a, smem, stream);
-    case MODE_DUMP: return launch_one<KIND, MODE_DUMP>(ta, tb, a, smem, stream);
-    case MODE_DUMP | MODE_LUT: return launch_one<KIND, MODE_DUMP | MODE_LUT>(ta, tb, a, smem, stream);
+  switch (a.Sy) {
+    case 2: return launch_sy<KIND, 2>(ta, tb, a, mode, smem, stream);
+    case 3: return launch_sy<KIND, 3>(ta, tb, a, mode, smem, stream);
+    case 4: return launch_sy<KIND, 4>(ta, tb, a, mode, smem, stream);
+    case 5: return launch_sy<KIND, 5>(ta, tb, a, mode, smem, stream);
+    case 6: return launch_sy<KIND, 6>(ta, tb, a, mode, smem, stream);
+    case 7: return launch_sy<KIND, 7>(ta, tb, a, mode, smem, stream);
+    case 8: return launch_sy<KIND, 8>(ta, tb, a, mode, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
 
+int mvm_column_groups(int sy) { return column_groups(sy); }  // Sy * 16 * CG <= 256 columns per TMEM slot
+
 size_t mvm_smem_bytes(const MvmArgs& a) {
-  return 1024 + static_cast<size_t>(a.stages) * a.stage_bytes + sizeof(float) * kMvmBM * kMvmBN + sizeof(SmemCtl) +
+  return 1024 + static_cast<size_t>(a.stages) * a.stage_bytes + sizeof(SmemCtl) +
          (a.lut_smem ? static_cast<size_t>(a.Sy) * a.lut_len * sizeof(int32_t) : 0);
 }
 
