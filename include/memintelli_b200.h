@@ -154,12 +154,21 @@ int mib_adc_plan(const mib_slice_spec* x_spec, const mib_slice_spec* w_spec, con
  * a_scale [Kt][M]; b_planes [Sy][N][Kt*pp], b_scale [Kt][N]; both E4M3 or both FP16.
  * `adc_table` as returned by mib_adc_plan (NULL when none is needed).  `bias` (N)
  * may be NULL.  `acc_dump`, when non-NULL, receives the exact int32 slice-pair
- * sums acc[t][r][n] = sum_ij code_ij * m_i m_j c_i c_j of every tile t (test hook). */
+ * sums acc[t][r][n] = sum_ij code_ij * m_i m_j c_i c_j of every tile t (test hook).
+ * `workspace` / `workspace_floats`: split-K scratch sized by mib_mvm_workspace (may be NULL). */
 int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_slice_spec* x_spec,
             const void* b_planes, const float* b_scale, int64_t n, const mib_slice_spec* w_spec,
             const mib_k_geom* kg, const mib_device_spec* dev, int32_t operand_kind, const int32_t* adc_table,
             int32_t adc_table_len, float* y, const mib_out_layout* layout, const float* bias, int32_t* acc_dump,
-            cudaStream_t stream);
+            float* workspace, int64_t workspace_floats, cudaStream_t stream);
+
+/* Split-K workspace for mib_mvm, in floats (0 when the output tiles already fill the GPU).
+ * When fewer than ~3/4 of the 148 SMs would get an output tile, mib_mvm divides the K tiles
+ * into contiguous ranges, writes one fp32 partial output per range into `workspace`
+ * ([splits][M][N]) and adds them in a fixed order (deterministic).  A NULL or smaller
+ * workspace runs the MVM without splitting. */
+int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
+                      const mib_k_geom* kg, const mib_device_spec* dev, int64_t* floats_out);
 
 /* Reads and clears the device-side error flag of the current device (synchronises it).
  * Returns MIB_OK, or MIB_ERR_TIMEOUT when a kernel gave up a bounded wait. */

@@ -86,6 +86,8 @@ struct MvmArgs {
   int64_t rows_per_group, group_stride, row_stride, col_stride;
   const float* bias;
   int32_t* acc_dump;        // [Kt][M][N] or null
+  int32_t tiles_per_split;  // K tiles per CTA along grid z (== Kt without split-K)
+  float* partial;           // split-K: [splits][M][N] fp32 partial outputs, or null
 };
 
 cudaError_t slice_dense(const float* x, int64_t ld_batch, int64_t ld_row, SliceArgs a, cudaStream_t stream);
@@ -99,6 +101,9 @@ cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, int6
 void launch_block_exp(const float* bmax, float* bexp, int64_t n, cudaStream_t stream);
 void count_launch(int n = 1);
 size_t mvm_smem_bytes(const MvmArgs& a);
+cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, int64_t N, float* y,
+                                 int64_t rows_per_group, int64_t group_stride, int64_t row_stride,
+                                 int64_t col_stride, const float* bias, cudaStream_t stream);
 int mvm_column_groups(int sy);   // output tile width BN = 16 * mvm_column_groups(Sy)
 cudaError_t launch_mvm(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, int kind, int acc_mode,
                        cudaStream_t stream);

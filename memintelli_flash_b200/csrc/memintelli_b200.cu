@@ -259,6 +259,31 @@ int adc_plan(const SliceTab& tx, const SliceTab& tw, const mib_slice_spec* xs, c
   return MIB_OK;
 }
 
+// Split-K choice: when the output tiles fill less than ~3/4 of the 148 SMs, the K tiles are
+// divided into `splits` contiguous ranges (multiples of the flush group, so no scale block is
+// cut), each written as an fp32 partial and reduced afterwards.
+struct SplitPlan {
+  int splits = 1;
+  int tiles_per_split = 0;
+};
+
+SplitPlan split_plan(int64_t m, int64_t n, int64_t kt, int flush, int sy) {
+  SplitPlan sp;
+  sp.tiles_per_split = static_cast<int>(kt);
+  const int64_t bn = 16 * mib::mvm_column_groups(sy);
+  const int64_t ctas = ((n + bn - 1) / bn) * ((m + mib::kMvmBM - 1) / mib::kMvmBM);
+  const int64_t groups = (kt + flush - 1) / flush;
+  if (ctas * 4 >= 148 * 3 || groups < 2) return sp;
+  int64_t want = (148 + ctas - 1) / ctas;
+  if (want > groups) want = groups;
+  if (want > 32) want = 32;
+  const int64_t per = (groups + want - 1) / want;           // flush groups per split
+  sp.tiles_per_split = static_cast<int>(per * flush);
+  sp.splits = static_cast<int>((kt + sp.tiles_per_split - 1) / sp.tiles_per_split);
+  if (sp.splits < 2) sp = SplitPlan{1, static_cast<int>(kt)};
+  return sp;
+}
+
 }  // namespace
 
 extern "C" {
@@ -452,11 +477,24 @@ int mib_adc_plan(const mib_slice_spec* x_spec, const mib_slice_spec* w_spec, con
   return MIB_OK;
 }
 
+int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
+                      const mib_k_geom* kg, const mib_device_spec* dev, int64_t* floats_out) {
+  SliceTab tx, tw;
+  if (int r = make_tab(x_spec, tx)) return r;
+  if (int r = make_tab(w_spec, tw)) return r;
+  if (!kg || !dev || !floats_out) return fail(MIB_ERR_PARAM, "NULL argument");
+  AdcPlan pl;
+  if (int r = adc_plan(tx, tw, x_spec, w_spec, kg, dev, pl)) return r;
+  const SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S);
+  *floats_out = sp.splits > 1 ? static_cast<int64_t>(sp.splits) * m * n : 0;
+  return MIB_OK;
+}
+
 int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_slice_spec* x_spec,
             const void* b_planes, const float* b_scale, int64_t n, const mib_slice_spec* w_spec,
             const mib_k_geom* kg, const mib_device_spec* dev, int32_t operand_kind, const int32_t* adc_table,
             int32_t adc_table_len, float* y, const mib_out_layout* layout, const float* bias, int32_t* acc_dump,
-            cudaStream_t stream) {
+            float* workspace, int64_t workspace_floats, cudaStream_t stream) {
   SliceTab tx, tw;
   if (int r = make_tab(x_spec, tx)) return r;
   if (int r = make_tab(w_spec, tw)) return r;
@@ -516,6 +554,7 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
       off += static_cast<uint32_t>(wij) * mib::kMagicBits;
     }
   a.tile_offset = off;
+
   a.out_scale = static_cast<float>(static_cast<double>(kg->p) / static_cast<double>(pl.R[0]));
   a.xs = a_scale;
   a.ws = b_scale;
@@ -526,11 +565,21 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   a.col_stride = layout->col_stride;
   a.bias = bias;
   a.acc_dump = acc_dump;
+  SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S);
+  if (sp.splits > 1 && (!workspace || workspace_floats < static_cast<int64_t>(sp.splits) * m * n))
+    sp = SplitPlan{1, static_cast<int>(kg->kt)};
+  a.tiles_per_split = sp.tiles_per_split;
+  a.partial = sp.splits > 1 ? workspace : nullptr;
   CUtensorMap ta, tb;
   if (int r = encode_planes(&ta, a_planes, operand_kind, m, kg->kt * kg->pp, tx.S, kg->pp, mib::kMvmBM)) return r;
   if (int r = encode_planes(&tb, b_planes, operand_kind, n, kg->kt * kg->pp, tw.S, kg->pp, bn)) return r;
   cudaError_t e = mib::launch_mvm(ta, tb, a, operand_kind, mode, stream);
   if (e != cudaSuccess) return cuda_fail(e, "mvm launch");
+  if (a.partial) {
+    e = mib::launch_splitk_reduce(a.partial, sp.splits, m, n, y, a.rows_per_group, a.group_stride, a.row_stride,
+                                  a.col_stride, bias, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
+  }
   return MIB_OK;
 }
 

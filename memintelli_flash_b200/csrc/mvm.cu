@@ -46,6 +46,16 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, ok);
 }
 
+// Two fp32 fused multiply-adds in one instruction (sm_100 f32x2): d = a * b + c on packed pairs.
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t pack2(uint32_t lo, uint32_t hi) {
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+
 // 32 lanes x 16 consecutive 32-bit columns -> 16 registers per thread.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -59,11 +69,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
 
 __host__ __device__ constexpr int column_groups(int sy) { return 16 / sy > 4 ? 4 : (16 / sy < 2 ? 2 : 16 / sy); }
 
-#ifndef MIB_USE_FFMA2
-#define MIB_USE_FFMA2 1
-#endif
-
-template <int KIND, int MODE, int SY>
+template <int KIND, int MODE, int SY, bool SPLIT>
 __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     mvm_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const __grid_constant__ MvmArgs P) {
@@ -86,7 +92,10 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kMvmBM;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
   constexpr int Sy = SY;
-  const int Sx = P.Sx, Kt = static_cast<int>(P.Kt), stages = P.stages;
+  const int Sx = P.Sx, stages = P.stages;
+  // split-K: this CTA covers K tiles [t_begin, t_begin + Kt)
+  const int t_begin = SPLIT ? static_cast<int>(blockIdx.z) * P.tiles_per_split : 0;
+  const int Kt = SPLIT ? min(P.tiles_per_split, static_cast<int>(P.Kt) - t_begin) : static_cast<int>(P.Kt);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -128,8 +137,8 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
         uint8_t* a_dst = smem + static_cast<size_t>(s) * P.stage_bytes;
         uint8_t* b_dst = a_dst + static_cast<size_t>(Sx) * P.a_slice_bytes;
         mbar_arrive_expect_tx(&ctl->full[s], P.stage_bytes);
-        tma_load_3d(a_dst, &tma_a, &ctl->full[s], t * P.pp, static_cast<int>(m0), 0);
-        tma_load_3d(b_dst, &tma_b, &ctl->full[s], t * P.pp, static_cast<int>(n0), 0);
+        tma_load_3d(a_dst, &tma_a, &ctl->full[s], (t_begin + t) * P.pp, static_cast<int>(m0), 0);
+        tma_load_3d(b_dst, &tma_b, &ctl->full[s], (t_begin + t) * P.pp, static_cast<int>(n0), 0);
         issued = t + 1;
         if (++s == stages) {
           s = 0;
@@ -192,9 +201,11 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     const int cg = (warp >> 2) * 16;    // 16-column group inside each weight slice's BN columns
     const int64_t row = m0 + q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cg;
-    float cj[8];
+    // ADC constants (radc_j - 1) / D, duplicated into f32x2 pairs, and the rounding constant pair
+    uint64_t cj2[SY];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) cj[j] = P.cadc[j];
+    for (int j = 0; j < SY; ++j) cj2[j] = pack2(__float_as_uint(P.cadc[j]), __float_as_uint(P.cadc[j]));
+    const uint64_t magic2 = pack2(kMagicBits, kMagicBits);
     uint32_t acc[16];
     float out[16];
 #pragma unroll
@@ -250,31 +261,18 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
                     acc[c] += wi[j] * static_cast<uint32_t>(code);
                 }
               } else {
-#if MIB_USE_FFMA2
-                const float2 cc = make_float2(cj[j], cj[j]);
-                const float2 mm = make_float2(kMagic, kMagic);
 #pragma unroll
                 for (int c = 0; c < 16; c += 2) {
-                  const float2 tq =
-                      __ffma2_rn(make_float2(__uint_as_float(r[jj][c]), __uint_as_float(r[jj][c + 1])), cc, mm);
+                  const uint64_t tq = ffma2(pack2(r[jj][c], r[jj][c + 1]), cj2[j], magic2);
+                  const uint32_t tx = static_cast<uint32_t>(tq), ty = static_cast<uint32_t>(tq >> 32);
                   if constexpr (kFloatAcc) {
-                    acc[c] = __float_as_uint(fmaf(tq.x - kMagic, wfi[j], __uint_as_float(acc[c])));
-                    acc[c + 1] = __float_as_uint(fmaf(tq.y - kMagic, wfi[j], __uint_as_float(acc[c + 1])));
+                    acc[c] = __float_as_uint(fmaf(__uint_as_float(tx) - kMagic, wfi[j], __uint_as_float(acc[c])));
+                    acc[c + 1] = __float_as_uint(fmaf(__uint_as_float(ty) - kMagic, wfi[j], __uint_as_float(acc[c + 1])));
                   } else {
-                    acc[c] += wi[j] * __float_as_uint(tq.x);
-                    acc[c + 1] += wi[j] * __float_as_uint(tq.y);
+                    acc[c] += wi[j] * tx;
+                    acc[c + 1] += wi[j] * ty;
                   }
                 }
-#else
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                  const float tq = fmaf(__uint_as_float(r[jj][c]), cj[j], kMagic);
-                  if constexpr (kFloatAcc)
-                    acc[c] = __float_as_uint(fmaf(tq - kMagic, wfi[j], __uint_as_float(acc[c])));
-                  else
-                    acc[c] += wi[j] * __float_as_uint(tq);
-                }
-#endif
               }
             }
           }
@@ -287,10 +285,11 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       if (!ok) break;
       ++cnt;
       if (kDump || cnt == P.flush_tiles || t == Kt - 1) {
-        const float xsv = row < P.M ? __ldg(P.xs + static_cast<int64_t>(t) * P.M + row) : 0.0f;
+        const int tg = t_begin + t;   // global K tile
+        const float xsv = row < P.M ? __ldg(P.xs + static_cast<int64_t>(tg) * P.M + row) : 0.0f;
         const float rs = kFloatAcc ? xsv : xsv * P.out_scale;
         const uint32_t off = (kLut || kFloatAcc) ? 0u : static_cast<uint32_t>(cnt) * P.tile_offset;
-        const float* wsr = P.ws + static_cast<int64_t>(t) * P.N + n0 + cg;
+        const float* wsr = P.ws + static_cast<int64_t>(tg) * P.N + n0 + cg;
 #pragma unroll
         for (int c = 0; c < 16; ++c) {
           const bool in = n0 + cg + c < P.N;
@@ -301,7 +300,7 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
           } else {
             const int32_t iv = static_cast<int32_t>(acc[c] - off);
             if constexpr (kDump) {
-              if (row < P.M && in) P.acc_dump[(static_cast<int64_t>(t) * P.M + row) * P.N + n0 + cg + c] = iv;
+              if (row < P.M && in) P.acc_dump[(static_cast<int64_t>(tg) * P.M + row) * P.N + n0 + cg + c] = iv;
             }
             v = static_cast<float>(iv);
           }
@@ -311,7 +310,14 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
         cnt = 0;
       }
     }
-    if (ok && row < P.M) {
+    if (SPLIT && ok && row < P.M) {
+      float* pr = P.partial + (static_cast<int64_t>(blockIdx.z) * P.M + row) * P.N;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const int64_t n = n0 + cg + c;
+        if (n < P.N) pr[n] = out[c];
+      }
+    } else if (ok && row < P.M) {
       const int64_t grp = row / P.rows_per_group;
       const int64_t rr = row - grp * P.rows_per_group;
       float* yb = P.y + grp * P.group_stride + rr * P.row_stride;
@@ -330,10 +336,10 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   }
 }
 
-template <int KIND, int MODE, int SY>
+template <int KIND, int MODE, int SY, bool SPLIT>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, size_t smem,
                        cudaStream_t stream) {
-  auto fn = mvm_kernel<KIND, MODE, SY>;
+  auto fn = mvm_kernel<KIND, MODE, SY, SPLIT>;
   static bool configured = false;  // per template instance; the smem cap is the same for every call
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -342,22 +348,30 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const MvmAr
   }
   constexpr int CG = column_groups(SY);
   constexpr int BN = 16 * CG;
-  dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + kMvmBM - 1) / kMvmBM));
+  const unsigned splits = SPLIT ? static_cast<unsigned>((a.Kt + a.tiles_per_split - 1) / a.tiles_per_split) : 1u;
+  dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + kMvmBM - 1) / kMvmBM), splits);
   fn<<<grid, 32 * (4 * CG + 2), smem, stream>>>(ta, tb, a);
   count_launch();
   return cudaGetLastError();
+}
+
+template <int KIND, int MODE, int SY>
+cudaError_t launch_split(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, size_t smem,
+                         cudaStream_t stream) {
+  if (a.partial) return launch_one<KIND, MODE, SY, true>(ta, tb, a, smem, stream);
+  return launch_one<KIND, MODE, SY, false>(ta, tb, a, smem, stream);
 }
 
 template <int KIND, int SY>
 cudaError_t launch_sy(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, int mode, size_t smem,
                       cudaStream_t stream) {
   switch (mode) {
-    case 0: return launch_one<KIND, 0, SY>(ta, tb, a, smem, stream);
-    case MODE_LUT: return launch_one<KIND, MODE_LUT, SY>(ta, tb, a, smem, stream);
-    case MODE_FLOATACC: return launch_one<KIND, MODE_FLOATACC, SY>(ta, tb, a, smem, stream);
-    case MODE_LUT | MODE_FLOATACC: return launch_one<KIND, MODE_LUT | MODE_FLOATACC, SY>(ta, tb, a, smem, stream);
-    case MODE_DUMP: return launch_one<KIND, MODE_DUMP, SY>(ta, tb, a, smem, stream);
-    case MODE_DUMP | MODE_LUT: return launch_one<KIND, MODE_DUMP | MODE_LUT, SY>(ta, tb, a, smem, stream);
+    case 0: return launch_split<KIND, 0, SY>(ta, tb, a, smem, stream);
+    case MODE_LUT: return launch_split<KIND, MODE_LUT, SY>(ta, tb, a, smem, stream);
+    case MODE_FLOATACC: return launch_split<KIND, MODE_FLOATACC, SY>(ta, tb, a, smem, stream);
+    case MODE_LUT | MODE_FLOATACC: return launch_split<KIND, MODE_LUT | MODE_FLOATACC, SY>(ta, tb, a, smem, stream);
+    case MODE_DUMP: return launch_split<KIND, MODE_DUMP, SY>(ta, tb, a, smem, stream);
+    case MODE_DUMP | MODE_LUT: return launch_split<KIND, MODE_DUMP | MODE_LUT, SY>(ta, tb, a, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -377,7 +391,35 @@ cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const MvmA
   }
 }
 
+// Split-K reduction: y[layout(r, n)] = sum_s partial[s][r][n] + bias[n], splits added in order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int64_t M, int64_t N,
+                                     float* __restrict__ y, int64_t rows_per_group, int64_t group_stride,
+                                     int64_t row_stride, int64_t col_stride, const float* __restrict__ bias) {
+  const int64_t total = M * N;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = e / N, n = e - (e / N) * N;
+    float v = 0.0f;
+    for (int s = 0; s < splits; ++s) v += __ldg(partial + static_cast<int64_t>(s) * total + e);
+    if (bias) v += __ldg(bias + n);
+    const int64_t grp = r / rows_per_group, rr = r - grp * rows_per_group;
+    y[grp * group_stride + rr * row_stride + n * col_stride] = v;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, int64_t N, float* y,
+                                 int64_t rows_per_group, int64_t group_stride, int64_t row_stride,
+                                 int64_t col_stride, const float* bias, cudaStream_t stream) {
+  const int64_t total = M * N;
+  int64_t blocks = (total + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  splitk_reduce_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(partial, splits, M, N, y, rows_per_group,
+                                                                          group_stride, row_stride, col_stride, bias);
+  count_launch();
+  return cudaGetLastError();
+}
 
 int mvm_column_groups(int sy) { return column_groups(sy); }  // Sy * 16 * CG <= 256 columns per TMEM slot
 

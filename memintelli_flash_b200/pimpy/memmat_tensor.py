@@ -83,6 +83,7 @@ class DPETensor(object):
         # as in the reference.  Tests set "cpu" to reproduce a CPU reference run's faults.
         self.fault_field_device = None
         self._plans = {}
+        self._ws_floats = {}
         # When a list, every fused MVM launch appends (start_event, end_event, slice_pair_ops,
         # adc_events) recorded on the launching stream (used by the benchmark's roofline).
         self.launch_log = None
@@ -295,6 +296,13 @@ class DPETensor(object):
                    b_planes.numel(), dspec, seed, 0, stream)
             a_planes, b_planes, kind = a16, b16, N.OPERAND_FP16
         mode, table, tlen = self._plan(xs, ws, kg, dspec, dev)
+        wkey = (M, Nc, bytes(xs), bytes(ws), bytes(kg), bytes(dspec))
+        if wkey not in self._ws_floats:
+            f = N.c_i64(0)
+            N.call("mib_mvm_workspace", M, Nc, xs, ws, kg, dspec, f)
+            self._ws_floats[wkey] = f.value
+        nws = self._ws_floats[wkey]
+        workspace = torch.empty(nws, dtype=torch.float32, device=dev) if nws else None
         if out is None:
             shape = (M, Nc) if gx["squeeze"] else (gx["batch"], gx["rows"], Nc)
             out = torch.empty(shape, dtype=torch.float32, device=dev)
@@ -307,7 +315,7 @@ class DPETensor(object):
             ev0.record()
         N.call("mib_mvm", N.ptr(a_planes), N.ptr(x._buf["tile_scale"]), M, xs, N.ptr(b_planes),
                N.ptr(mat._buf["tile_scale"]), Nc, ws, kg, dspec, kind, N.ptr(table), tlen, N.ptr(out), layout,
-               N.ptr(bias), N.ptr(acc_dump), stream)
+               N.ptr(bias), N.ptr(acc_dump), N.ptr(workspace), nws, stream)
         if log is not None:
             ev1.record()
             np_cols = gw["cols_p"]

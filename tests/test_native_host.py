@@ -83,6 +83,15 @@ def test_adc_plan_non_dyadic_needs_table():
     assert list(table)[:289] == [round(s * 1023 / 288) for s in range(289)]
 
 
+def test_split_k_workspace_choice():
+    xs, ws, kg, dev = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 32), (128, 128)), _kg(500), _dev(4096)
+    f = N.c_i64(-1)
+    assert N.lib().mib_mvm_workspace(400, 600, xs, ws, kg, dev, f) == 0
+    assert f.value > 0 and f.value % (400 * 600) == 0            # 52 output tiles: split the 16 K tiles
+    assert N.lib().mib_mvm_workspace(16384, 3072, xs, ws, _kg(1024), dev, f) == 0
+    assert f.value == 0                                           # 8192 output tiles: no split
+
+
 def test_adc_plan_noisy_skips_table():
     rc, mode, n = _plan(_spec(SM, (1, 32), (1, 64)), _spec(SM, (32, 32), (64, 64)), _kg(100, qg=64),
                         _dev(1024, sigma=0.05))
@@ -107,5 +116,5 @@ def test_slice_method_first_bit_checked():
 def test_mvm_rejects_bad_arguments_before_any_device_work():
     xs, ws = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 64), (128, 128))
     rc = N.lib().mib_mvm(None, None, 10, xs, None, None, 10, ws, _kg(128), _dev(4096), 0, None, 0, None, None,
-                         None, None, None)
+                         None, None, None, 0, None)
     assert rc == N.MIB_ERR_PARAM
