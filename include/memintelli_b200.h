@@ -170,6 +170,25 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
 int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
                       const mib_k_geom* kg, const mib_device_spec* dev, int64_t* floats_out);
 
+/* mib_mvm for callers that cannot allocate device memory: no counterpart in the reference
+ * (whose torch path allocates freely).  It is meant for runtimes without a CUDA allocator
+ * at hand and for callers that must not allocate while they run.  Same arguments and
+ * result as mib_mvm without the workspace (and without the acc_dump test hook).  When
+ * the output tiles fill less of the GPU than split-K needs, the split-K partials go to
+ * a scratch array built into this library: 2^20 floats (4 MiB), held on every GPU that
+ * loads the library until the process exits.  Problems whose split-K scratch
+ * (mib_mvm_workspace) exceeds 2^20 floats are rejected with MIB_ERR_UNSUPPORTED.
+ * The first call on a device resolves the array's device address (cudaGetSymbolAddress),
+ * so make that first call before any stream capture.  The array is shared by every call
+ * and keeps the last call's contents (every split overwrites all of its partials before
+ * they are read, so nothing needs clearing); calls that overlap on the GPU, e.g. on two
+ * streams, race on it. */
+int mib_mvm_static_scratch(const void* a_planes, const float* a_scale, int64_t m, const mib_slice_spec* x_spec,
+                           const void* b_planes, const float* b_scale, int64_t n, const mib_slice_spec* w_spec,
+                           const mib_k_geom* kg, const mib_device_spec* dev, int32_t operand_kind,
+                           const int32_t* adc_table, int32_t adc_table_len, float* y, const mib_out_layout* layout,
+                           const float* bias, cudaStream_t stream);
+
 /* Reads and clears the device-side error flag of the current device (synchronises it).
  * Returns MIB_OK, or MIB_ERR_TIMEOUT when a kernel gave up a bounded wait. */
 int mib_device_status(void);

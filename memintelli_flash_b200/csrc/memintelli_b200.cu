@@ -584,3 +584,64 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// mib_mvm_static_scratch: the fused MVM for callers that cannot allocate device memory
+// (an allocator-less runtime, a host without the CUDA allocator at hand, or a caller
+// that must not grow its memory footprint while running).  The split-K partial
+// outputs live in a fixed array compiled into this library instead of a
+// caller-provided workspace.
+// ---------------------------------------------------------------------------
+namespace {
+
+// Split-K scratch: 2^20 floats (4 MiB).  Every GPU that loads this library holds
+// this array until the process exits.
+constexpr int64_t kStaticScratchFloats = int64_t(1) << 20;
+static __device__ __align__(256) float g_static_scratch[kStaticScratchFloats];
+
+// Device address of g_static_scratch per device, resolved on the first call on that
+// device (with it current).  Host code must not pass the symbol itself to a kernel.
+std::mutex g_static_scratch_mu;
+float* g_static_scratch_ptr[128] = {};
+
+int static_scratch_address(float** out) {
+  int device = -1;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (device < 0 || device >= 128) return fail(MIB_ERR_CUDA, "device index out of range for the static scratch");
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (!g_static_scratch_ptr[device]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static split-K scratch)");
+    g_static_scratch_ptr[device] = static_cast<float*>(p);
+  }
+  *out = g_static_scratch_ptr[device];
+  return MIB_OK;
+}
+
+}  // namespace
+
+extern "C" int mib_mvm_static_scratch(const void* a_planes, const float* a_scale, int64_t m,
+                                      const mib_slice_spec* x_spec, const void* b_planes, const float* b_scale,
+                                      int64_t n, const mib_slice_spec* w_spec, const mib_k_geom* kg,
+                                      const mib_device_spec* dev, int32_t operand_kind, const int32_t* adc_table,
+                                      int32_t adc_table_len, float* y, const mib_out_layout* layout,
+                                      const float* bias, cudaStream_t stream) {
+  int64_t need = 0;
+  if (int r = mib_mvm_workspace(m, n, x_spec, w_spec, kg, dev, &need)) return r;
+  if (need > kStaticScratchFloats) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "this MVM needs %lld floats of split-K scratch but the built-in scratch holds %lld; "
+             "use mib_mvm with a caller-provided workspace",
+             static_cast<long long>(need), static_cast<long long>(kStaticScratchFloats));
+    return fail(MIB_ERR_UNSUPPORTED, buf);
+  }
+  float* scratch = nullptr;
+  if (need > 0) {
+    if (int r = static_scratch_address(&scratch)) return r;
+  }
+  return mib_mvm(a_planes, a_scale, m, x_spec, b_planes, b_scale, n, w_spec, kg, dev, operand_kind, adc_table,
+                 adc_table_len, y, layout, bias, nullptr, scratch, need > 0 ? kStaticScratchFloats : 0, stream);
+}
