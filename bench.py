@@ -34,6 +34,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "CIM Qwen3-0.6B-arch prefill tokens/s (8x2048, all 197 linears on the CIM engine)"
+# q/k/v and gate/up of a layer share their input and run as one crossbar array each (exact: output
+# columns are independent), so a forward launches 4 CIM matmuls per layer + lm_head.
 BATCH, SEQ = 8, 2048
 ENGINE = dict(HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0,
               read_variation=0.05, vnoise=0.0, rdac=4, g_level=4, radc=4096)

@@ -47,10 +47,11 @@ def _world(group):
 class _ShardBase(torch.nn.Module):
     def __init__(self, engine, weight: torch.Tensor, bias: Optional[torch.Tensor], dim: int, input_slice,
                  weight_slice, bw_e=None, input_paral_size=(1, 32), weight_paral_size=(32, 32),
-                 input_quant_gran=(1, 32), weight_quant_gran=(32, 32), group=None, device=None):
+                 input_quant_gran=(1, 32), weight_quant_gran=(32, 32), group=None, device=None,
+                 presharded: bool = False):
         super().__init__()
         self.group = group
-        world, rank = _world(group)
+        world, rank = (1, 0) if presharded else _world(group)
         out_f, in_f = weight.shape
         qg = weight_quant_gran if not isinstance(weight_quant_gran, str) else (in_f, out_f)
         if dim == 0:   # output columns of W^T == rows of the (out, in) weight
@@ -108,9 +109,37 @@ class _LinearFromWeight(LinearMem):
 
 class ColumnShardedLinearMem(_ShardBase):
     """Output columns split across ranks; ``forward`` returns this rank's columns
-    (``gather=True``: all-gathers the full output along the last dimension)."""
+    (``gather=True``: all-gathers the full output along the last dimension).
+
+    ``weight`` may be a list of (out_i, in) weights sharing one input (e.g. q/k/v):
+    each part is sharded on its own quant blocks and the local shards are
+    concatenated into one crossbar array, so one slicing of the input and one MVM
+    serve all parts; ``split_sizes`` gives the local width of every part.
+    """
 
     def __init__(self, engine, weight, bias, input_slice, weight_slice, gather=False, **kw):
+        if isinstance(weight, (list, tuple)):
+            if gather:
+                raise ValueError("gather is not supported for a fused multi-part weight")
+            group = kw.get("group")
+            world, rank = _world(group)
+            qg = kw.get("weight_quant_gran", (32, 32))
+            wp = kw.get("weight_paral_size", (32, 32))
+            blk = math.ceil(qg[1] / wp[1]) * wp[1]
+            parts = []
+            for w in weight:
+                if w.shape[0] % blk:
+                    raise ValueError("every fused part must be a whole number of weight quant blocks")
+                lo, hi = shard_bounds(w.shape[0], blk, world, rank)
+                parts.append(w[lo:hi])
+            self._fused_sizes = [p.shape[0] for p in parts]
+            fused = torch.cat(parts, dim=0)
+            super().__init__(engine, fused, bias, 0, input_slice, weight_slice, presharded=True, **kw)
+            self.group, self.world, self.rank = group, world, rank
+            self.gather = False
+            self.shard_sizes = None
+            return
+        self._fused_sizes = None
         super().__init__(engine, weight, bias, 0, input_slice, weight_slice, **kw)
         self.gather = gather
         qg = kw.get("weight_quant_gran", (32, 32))
@@ -118,6 +147,10 @@ class ColumnShardedLinearMem(_ShardBase):
         blk = math.ceil(qg[1] / wp[1]) * wp[1] if not isinstance(qg, str) else self.out_features
         self.shard_sizes = [b - a for a, b in (shard_bounds(self.out_features, blk, self.world, r)
                                                for r in range(self.world))]
+
+    @property
+    def split_sizes(self):
+        return self._fused_sizes
 
     def forward(self, x):
         y = self.local(x)

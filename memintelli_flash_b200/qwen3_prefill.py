@@ -89,27 +89,39 @@ class Qwen3CimLayer(torch.nn.Module):
 
         kw = dict(group=group, device=device, **spec.kwargs())
         sl = (spec.input_slice, spec.weight_slice)
-        self.q_proj = ColumnShardedLinearMem(engine, w(a.heads * a.head_dim, a.hidden), None, *sl, **kw)
-        self.k_proj = ColumnShardedLinearMem(engine, w(a.kv_heads * a.head_dim, a.hidden), None, *sl, **kw)
-        self.v_proj = ColumnShardedLinearMem(engine, w(a.kv_heads * a.head_dim, a.hidden), None, *sl, **kw)
+        # q/k/v and gate/up read the same input: their crossbars are programmed side by side
+        # (per rank: this rank's heads of q, k and v), so the input is sliced once per group.
+        # Output columns are independent in the CIM arithmetic, so this is exact.
+        self.qkv_proj = ColumnShardedLinearMem(
+            engine, [w(a.heads * a.head_dim, a.hidden), w(a.kv_heads * a.head_dim, a.hidden),
+                     w(a.kv_heads * a.head_dim, a.hidden)], None, *sl, **kw)
         self.o_proj = RowShardedLinearMem(engine, w(a.hidden, a.heads * a.head_dim), None, *sl, **kw)
-        self.gate_proj = ColumnShardedLinearMem(engine, w(a.intermediate, a.hidden), None, *sl, **kw)
-        self.up_proj = ColumnShardedLinearMem(engine, w(a.intermediate, a.hidden), None, *sl, **kw)
+        self.gate_up_proj = ColumnShardedLinearMem(
+            engine, [w(a.intermediate, a.hidden), w(a.intermediate, a.hidden)], None, *sl, **kw)
         self.down_proj = RowShardedLinearMem(engine, w(a.hidden, a.intermediate), None, *sl, **kw)
         self.in_norm = torch.nn.Parameter(torch.ones(a.hidden, device=device), requires_grad=False)
         self.post_norm = torch.nn.Parameter(torch.ones(a.hidden, device=device), requires_grad=False)
         self.q_norm = torch.nn.Parameter(torch.ones(a.head_dim, device=device), requires_grad=False)
         self.k_norm = torch.nn.Parameter(torch.ones(a.head_dim, device=device), requires_grad=False)
-        self.local_heads = self.q_proj.local.out_features // a.head_dim
-        self.local_kv = self.k_proj.local.out_features // a.head_dim
+        q_cols, k_cols, v_cols = self.qkv_proj.split_sizes
+        if q_cols % a.head_dim or k_cols % a.head_dim or k_cols == 0 or q_cols == 0:
+            raise ValueError(f"crossbar sharding must give every rank whole, non-empty heads "
+                             f"(local q columns {q_cols}, k columns {k_cols}, head_dim {a.head_dim})")
+        self.local_heads = q_cols // a.head_dim
+        self.local_kv = k_cols // a.head_dim
+        if self.local_heads % self.local_kv:
+            raise ValueError("each rank's query heads must be a multiple of its key/value heads")
+        self.local_inter = self.gate_up_proj.split_sizes[0]
 
     def forward(self, h, cos, sin):
         a = self.arch
         B, T, _ = h.shape
         x = rms_norm(h, self.in_norm, a.eps)
-        q = self.q_proj(x).view(B, T, self.local_heads, a.head_dim)
-        k = self.k_proj(x).view(B, T, self.local_kv, a.head_dim)
-        v = self.v_proj(x).view(B, T, self.local_kv, a.head_dim)
+        qkv = self.qkv_proj(x)
+        nq, nk = self.local_heads * a.head_dim, self.local_kv * a.head_dim
+        q = qkv[..., :nq].reshape(B, T, self.local_heads, a.head_dim)
+        k = qkv[..., nq:nq + nk].reshape(B, T, self.local_kv, a.head_dim)
+        v = qkv[..., nq + nk:].reshape(B, T, self.local_kv, a.head_dim)
         q = apply_rope(rms_norm(q, self.q_norm, a.eps), cos, sin).transpose(1, 2)
         k = apply_rope(rms_norm(k, self.k_norm, a.eps), cos, sin).transpose(1, 2)
         v = v.transpose(1, 2)
@@ -118,7 +130,8 @@ class Qwen3CimLayer(torch.nn.Module):
         o = o.transpose(1, 2).reshape(B, T, self.local_heads * a.head_dim).float()
         h = h + self.o_proj(o)
         x = rms_norm(h, self.post_norm, a.eps)
-        m = F.silu(self.gate_proj(x)) * self.up_proj(x)
+        gu = self.gate_up_proj(x)
+        m = F.silu(gu[..., :self.local_inter]) * gu[..., self.local_inter:]
         return h + self.down_proj(m)
 
 
@@ -147,7 +160,7 @@ class Qwen3CimPrefill(torch.nn.Module):
 
     def cim_linears(self):
         for layer in self.layers:
-            for name in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+            for name in ("qkv_proj", "o_proj", "gate_up_proj", "down_proj"):
                 yield getattr(layer, name).local
         yield self.lm_head.local
 

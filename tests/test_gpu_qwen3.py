@@ -1,0 +1,116 @@
+"""Qwen3-architecture CIM prefill on the GPU: fused crossbars and crossbar sharding (needs a B200).
+
+The multi-GPU case spawns 2 NCCL ranks and is skipped when fewer GPUs are visible.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+NOISE_FREE = dict(HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0,
+                  read_variation=0.0, vnoise=0.0, rdac=4, g_level=4, radc=4096)
+# every q/k/v part is a whole number of 128-column quant blocks per rank for 1 and 2 ranks
+SMALL = dict(hidden=256, layers=2, heads=4, kv_heads=2, head_dim=128, intermediate=512, vocab=1000)
+
+
+def test_fused_columns_equal_separate_linears(cuda):
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200.crossbar_shard import ColumnShardedLinearMem, _LinearFromWeight
+    eng = M.DPETensor(device=cuda, **NOISE_FREE)
+    g = torch.Generator(device=cuda).manual_seed(3)
+    wq, wk, wv = (torch.randn(n, 256, generator=g, device=cuda) * 0.05 for n in (256, 128, 128))
+    kw = dict(input_paral_size=(1, 32), weight_paral_size=(32, 32), input_quant_gran=(1, 128),
+              weight_quant_gran=(128, 128), device=cuda)
+    fused = ColumnShardedLinearMem(eng, [wq, wk, wv], None, (1, 1, 2, 2, 2), (1, 1, 2, 2, 2), **kw)
+    x = torch.randn(3, 50, 256, generator=g, device=cuda)
+    y = fused(x)
+    outs = []
+    for w in (wq, wk, wv):
+        lin = _LinearFromWeight(eng, w, None, (1, 1, 2, 2, 2), (1, 1, 2, 2, 2), None, (1, 32), (32, 32),
+                                (1, 128), (128, 128), cuda)
+        outs.append(lin(x))
+    ref = torch.cat(outs, dim=-1)
+    torch.cuda.synchronize()
+    assert fused.split_sizes == [256, 128, 128]
+    a, b = y.double().cpu().numpy(), ref.double().cpu().numpy()
+    assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-6
+
+
+def test_small_model_forward(cuda):
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
+    eng = M.DPETensor(device=cuda, **NOISE_FREE)
+    model = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=cuda)
+    ids = torch.randint(0, SMALL["vocab"], (2, 64), generator=torch.Generator().manual_seed(2)).to(cuda)
+    loss = float(model(ids))
+    assert np.isfinite(loss) and abs(loss - np.log(SMALL["vocab"])) < 1.0
+    assert loss == float(model(ids))           # noise-free: deterministic
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _shard_worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import datetime
+    import torch.distributed as dist
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=120))
+    eng = M.DPETensor(device=dev, **NOISE_FREE)
+    ids = torch.randint(0, SMALL["vocab"], (2, 64), generator=torch.Generator().manual_seed(2)).to(dev)
+    sharded = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=dev)
+    loss_sharded = float(sharded(ids))
+    dist.barrier()
+    if rank == 0:
+        solo = dist.new_group([0])
+    else:
+        dist.new_group([0])
+    if rank == 0:
+        single = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=dev, group=solo)
+        q.put((loss_sharded, float(single(ids))))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_crossbar_sharded_model_matches_single_gpu():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_shard_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    import queue
+    import time
+    t0 = time.time()
+    while True:                                   # fail fast if a rank dies
+        try:
+            loss_sharded, loss_single = q.get(timeout=2)
+            break
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            if dead or time.time() - t0 > 240:
+                for p in procs:
+                    if p.is_alive():
+                        p.kill()
+                pytest.fail(f"a rank exited with {dead} or the test timed out")
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert abs(loss_sharded - loss_single) < 1e-5 * abs(loss_single)
