@@ -12,6 +12,8 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <type_traits>
+
 namespace mib {
 
 static unsigned long long g_launches = 0;
@@ -82,9 +84,98 @@ __global__ void block_absmax_kernel(Loader ld, int64_t batch, int64_t rows, int6
 // input slicing: one warp per (b, row, column quant block).  When `have_max`
 // is false the block is one row high (quant_gran[0] == 1) and the warp computes
 // its max itself, making the kernel a single pass over x.
+//
+// The DAC level of slice t is round(code_t / m_t * (rdac - 1)) with the
+// reference's fp32 steps; it depends only on the packed code q (< 2^bits), so
+// each CTA tabulates q -> encoded level of every slice once in shared memory.
 // ---------------------------------------------------------------------------
+// Quantise one value to its packed code given the block maximum / exponent.
+// inv_p2e = 2^-e when that is a normal float (e <= 126): v / 2^e == v * 2^-e then, both being one
+// correctly rounded operation on the same real value.  Otherwise inv_p2e is 0 and the division runs.
+__device__ __forceinline__ int quantize_fast(float v, float bmax, int e, float inv_p2e, int bits, bool bfp) {
+  int q;
+  if (bfp) {
+    const float s = inv_p2e != 0.0f ? __fmul_rn(v, inv_p2e) : __fdiv_rn(v, pow2f(e));
+    float t = __fmul_rn(s, static_cast<float>(1 << (bits - 2)));
+    float r = rintf(t);
+    r = fminf(fmaxf(r, -static_cast<float>(1 << (bits - 1))), static_cast<float>((1 << (bits - 1)) - 1));
+    q = static_cast<int>(r);
+  } else {
+    if (bmax == 0.0f) return 0;
+    q = static_cast<int>(rintf(__fmul_rn(__fdiv_rn(v, bmax), static_cast<float>((1 << (bits - 1)) - 1))));
+  }
+  if (q < 0) q += (1 << bits);
+  return q;
+}
+
+// Per-CTA table: packed code q -> encoded level of every slice.  E4M3 keeps slice t in byte t&3 of
+// word t>>2; FP16 keeps it in half t&1 of word t>>1.
+template <int KIND>
+struct LevelLut {
+  static constexpr int kWords = KIND == MIB_OPERAND_E4M3 ? 2 : 4;
+  uint32_t w[256][kWords];
+};
+
+template <int KIND>
+__device__ __forceinline__ void build_level_lut(LevelLut<KIND>& lut, const SliceArgs& a) {
+  for (int q = threadIdx.x; q < (1 << a.bits); q += blockDim.x) {
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    for (int t = 0; t < a.n_slices; ++t) {
+      const int code = (q >> a.offs[t]) & a.maxes[t];
+      const float lv = static_cast<float>(level_map(code, a.maxes[t], a.lm1));
+      if constexpr (KIND == MIB_OPERAND_E4M3) {
+        w[t >> 2] |= static_cast<uint32_t>(enc_e4m3(lv)) << (8 * (t & 3));
+      } else {
+        const __half h = __float2half_rn(lv);
+        w[t >> 1] |= static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(&h)) << (16 * (t & 1));
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < LevelLut<KIND>::kWords; ++k) lut.w[q][k] = w[k];
+  }
+  __syncthreads();
+}
+
+// Write the planes of 4 consecutive positions (codes q0..q3) starting at element offset dst.
+// S > 0 fixes the slice count at compile time; S == 0 reads it from the arguments.
+template <int KIND, int S>
+__device__ __forceinline__ void store_planes4(const LevelLut<KIND>& lut, const SliceArgs& a, int64_t dst, int q0,
+                                              int q1, int q2, int q3) {
+  const int ns = S > 0 ? S : a.n_slices;
+  if constexpr (KIND == MIB_OPERAND_E4M3) {
+    const uint32_t lo0 = lut.w[q0][0], lo1 = lut.w[q1][0], lo2 = lut.w[q2][0], lo3 = lut.w[q3][0];
+    uint32_t hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
+    if (S == 0 || S > 4) hi0 = lut.w[q0][1], hi1 = lut.w[q1][1], hi2 = lut.w[q2][1], hi3 = lut.w[q3][1];
+    uint8_t* base = static_cast<uint8_t*>(a.planes) + dst;
+#pragma unroll
+    for (int t = 0; t < (S > 0 ? S : 8); ++t) {
+      if (S == 0 && t >= ns) break;
+      const uint32_t k = static_cast<uint32_t>(t & 3);
+      const bool lo = t < 4;
+      const uint32_t p01 = __byte_perm(lo ? lo0 : hi0, lo ? lo1 : hi1, k | ((k + 4) << 4));
+      const uint32_t p23 = __byte_perm(lo ? lo2 : hi2, lo ? lo3 : hi3, k | ((k + 4) << 4));
+      *reinterpret_cast<uint32_t*>(base + t * a.plane_stride) = __byte_perm(p01, p23, 0x5410);
+    }
+  } else {
+    __half* base = static_cast<__half*>(a.planes) + dst;
+#pragma unroll
+    for (int t = 0; t < (S > 0 ? S : 8); ++t) {
+      if (S == 0 && t >= ns) break;
+      const int wk = t >> 1;
+      const uint32_t sel = (t & 1) ? 0x7632u : 0x5410u;
+      uint2 o;
+      o.x = __byte_perm(lut.w[q0][wk], lut.w[q1][wk], sel);
+      o.y = __byte_perm(lut.w[q2][wk], lut.w[q3][wk], sel);
+      *reinterpret_cast<uint2*>(base + t * a.plane_stride) = o;
+    }
+  }
+}
+
 template <class Loader, int KIND>
 __global__ void slice_rows_kernel(Loader ld, SliceArgs a, bool have_max) {
+  __shared__ LevelLut<KIND> lut;
+  build_level_lut<KIND>(lut, a);
+
   const int lane = threadIdx.x & 31;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int64_t nitems = a.batch * a.rows * a.nbc;
@@ -109,41 +200,152 @@ __global__ void slice_rows_kernel(Loader ld, SliceArgs a, bool have_max) {
     }
     const int e = a.bfp ? bfp_exponent(bm) : 0;
     if (a.bfp && lane == 0 && !have_max && a.block_exp) a.block_exp[blk] = static_cast<float>(e);
+    const float inv_p2e = (a.bfp && e <= 126) ? pow2f(-e) : 0.0f;
     const float scale = a.bfp ? pow2f(e + 2 - a.bits) : bm / static_cast<float>((1 << (a.bits - 1)) - 1);
     const int64_t tile0 = cb * tiles_per_block;
     const int64_t npos = static_cast<int64_t>(tiles_per_block) * a.pp;
-    const int64_t plane_row = (b * a.rows + r) * a.row_pitch;
+    const int64_t row_idx = b * a.rows + r;
+    const int64_t plane_row = row_idx * a.row_pitch;
     for (int64_t pos = 4 * lane; pos < npos; pos += 128) {
       int q[4];
+      const int64_t tt = pos / a.pp;                    // 4 positions never straddle a tile (pp % 4 == 0)
+      const int o0 = static_cast<int>(pos - tt * a.pp);
+      const int64_t c0 = (tile0 + tt) * a.p + o0;
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const int64_t tp = pos + u;
-        const int64_t tt = tp / a.pp;
-        const int o = static_cast<int>(tp - tt * a.pp);
-        const int64_t c = (tile0 + tt) * a.p + o;
-        const float v = (o < a.p) ? ld(b, r, c) : 0.0f;
-        q[u] = (o < a.p) ? quantize(v, bm, e, a.bits, a.bfp) : 0;
-        if (o == 0) a.tile_scale[(tile0 + tt) * a.scale_ld + (b * a.rows + r)] = scale;
-        if (a.packed && o < a.p) a.packed[(b * a.rows + r) * a.kp + c] = static_cast<uint8_t>(q[u]);
+        const bool real = o0 + u < a.p;
+        q[u] = real ? quantize_fast(ld(b, r, c0 + u), bm, e, inv_p2e, a.bits, a.bfp) : 0;
       }
-      const int64_t dst = plane_row + tile0 * a.pp + pos;
-      for (int t = 0; t < a.n_slices; ++t) {
-        float lv[4];
+      if (o0 == 0) a.tile_scale[(tile0 + tt) * a.scale_ld + row_idx] = scale;
+      if (a.packed) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int code = (q[u] >> a.offs[t]) & a.maxes[t];
-          lv[u] = static_cast<float>(level_map(code, a.maxes[t], a.lm1));
-        }
-        if constexpr (KIND == MIB_OPERAND_E4M3) {
-          uchar4 o4 = make_uchar4(enc_e4m3(lv[0]), enc_e4m3(lv[1]), enc_e4m3(lv[2]), enc_e4m3(lv[3]));
-          *reinterpret_cast<uchar4*>(static_cast<uint8_t*>(a.planes) + t * a.plane_stride + dst) = o4;
-        } else {
-          __half2 h01 = __floats2half2_rn(lv[0], lv[1]), h23 = __floats2half2_rn(lv[2], lv[3]);
-          __half2* p2 = reinterpret_cast<__half2*>(static_cast<__half*>(a.planes) + t * a.plane_stride + dst);
-          p2[0] = h01;
-          p2[1] = h23;
-        }
+        for (int u = 0; u < 4; ++u)
+          if (o0 + u < a.p) a.packed[row_idx * a.kp + c0 + u] = static_cast<uint8_t>(q[u]);
       }
+      store_planes4<KIND, 0>(lut, a, plane_row + tile0 * a.pp + pos, q[0], q[1], q[2], q[3]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Vectorised input slicing for dense rows: unit column stride, 16-byte aligned rows, K % 4 == 0
+// and unpadded tiles (pp == p, so plane positions are columns).  Work item = (row, group of
+// kChunks chunks of 128 columns); lane l of a chunk holds columns 4l..4l+3 as one float4, so a
+// warp keeps kChunks * 512 bytes of x in flight.  Without precomputed maxima (one-row quant
+// blocks, qg1 dividing 128) the block max is a butterfly over the qg1/4 lanes of the block.
+// The BFP exponent (a double-precision log2) is evaluated by one lane per block and broadcast.
+// ---------------------------------------------------------------------------
+constexpr int kSliceVecChunks = 4;
+
+// rne(t) for |t| < 2^22 on the FMA pipe: adding 1.5 * 2^23 leaves the rounded integer in the low mantissa bits.
+__device__ __forceinline__ int rne_small(float t) {
+  return __float_as_int(__fadd_rn(t, 12582912.0f)) - 0x4B400000;
+}
+
+// fl(v / b) for |v| <= b and 2^-60 <= b < 2^126, given rb = RN(1/b), without a per-element division.
+// y0 = RN(v * rb) is within 1.5 ulp of v/b; one residual correction y1 = RN(y0 + rb * (v - b * y0)) brings it
+// well within one ulp, and the same step once more is Markstein's final correction (P. Markstein, IBM J. Res.
+// Dev. 34(1):111-119, 1990), which returns RN(v / b) when rb = RN(1/b) and the estimate is within one ulp.
+// The residuals v - b * y are exact under FMA for these magnitudes (no underflow since b >= 2^-60).
+__device__ __forceinline__ float div_markstein(float v, float b, float rb) {
+  float y = __fmul_rn(v, rb);
+  float r = __fmaf_rn(-b, y, v);
+  y = __fmaf_rn(r, rb, y);
+  r = __fmaf_rn(-b, y, v);
+  return __fmaf_rn(r, rb, y);
+}
+
+// quantize() for the vector path.  INT: rne(fl(fl(v / bmax) * qmax)), |t| <= qmax; the division uses
+// div_markstein when rb != 0 (bmax in its range), else __fdiv_rn.  BFP: v / 2^e as quantize_fast,
+// |t| <= 2^(bits-1).  Both stay far below 2^22, so rne_small rounds exactly.
+__device__ __forceinline__ int quantize_vec(float v, float bmax, float rb, float qmax, int e, float inv_p2e, int bits,
+                                            bool bfp) {
+  int q;
+  if (bfp) {
+    const float s = inv_p2e != 0.0f ? __fmul_rn(v, inv_p2e) : __fdiv_rn(v, pow2f(e));
+    q = rne_small(__fmul_rn(s, static_cast<float>(1 << (bits - 2))));
+    q = min(max(q, -(1 << (bits - 1))), (1 << (bits - 1)) - 1);
+  } else if (rb != 0.0f) {
+    q = rne_small(__fmul_rn(div_markstein(v, bmax, rb), qmax));
+  } else {
+    q = bmax == 0.0f ? 0 : rne_small(__fmul_rn(__fdiv_rn(v, bmax), qmax));
+  }
+  return q & ((1 << bits) - 1);
+}
+
+template <int KIND, int S>
+__global__ void __launch_bounds__(256, 4) slice_dense_vec_kernel(const float* __restrict__ x, int64_t ld_batch,
+                                                                 int64_t ld_row, SliceArgs a, bool have_max) {
+  __shared__ LevelLut<KIND> lut;
+  build_level_lut<KIND>(lut, a);
+
+  const int lane = threadIdx.x & 31;
+  const int nwarps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
+  const int nrows = static_cast<int>(a.batch * a.rows);
+  const int rows = static_cast<int>(a.rows);
+  const int kp = static_cast<int>(a.kp), cols = static_cast<int>(a.cols);
+  const int nchunks = (kp + 127) / 128;
+  const int ngroups = (nchunks + kSliceVecChunks - 1) / kSliceVecChunks;
+  const int nitems = nrows * ngroups;
+  const int lp = __ffs(a.p) - 1, lq = __ffs(a.qg1) - 1;  // p and qg1 are powers of two here
+  // lanes sharing one quant block inside a chunk: qg1/4 when qg1 divides 128, else the whole warp
+  const int glanes = a.qg1 <= 128 ? a.qg1 / 4 : 32;
+  const int leader = lane & ~(glanes - 1);
+  const float qmax = static_cast<float>((1 << (a.bits - 1)) - 1);
+  for (int item = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < nitems; item += nwarps) {
+    const int row_idx = item / ngroups;
+    const int ch0 = (item - row_idx * ngroups) * kSliceVecChunks;
+    const int b = row_idx / rows, r = row_idx - b * rows;
+    const float* xr = x + b * ld_batch + static_cast<int64_t>(r) * ld_row;
+    const int64_t blk_row = (static_cast<int64_t>(b) * a.nbr + (a.qg0 == 1 ? r : r / a.qg0)) * a.nbc;
+    float4 v[kSliceVecChunks];
+#pragma unroll
+    for (int u = 0; u < kSliceVecChunks; ++u) {
+      const int col = (ch0 + u) * 128 + 4 * lane;
+      v[u] = col < cols ? __ldg(reinterpret_cast<const float4*>(xr + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < kSliceVecChunks; ++u) {
+      if (ch0 + u >= nchunks) break;  // warp-uniform
+      const int col = (ch0 + u) * 128 + 4 * lane;
+      const bool valid = col < kp;
+      const int cb = col >> lq;
+      float bm;
+      if (have_max) {
+        bm = valid ? a.block_max[blk_row + cb] : 0.0f;
+      } else {
+        float m = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+          if (o < glanes) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bm = m;
+      }
+      int e = 0;
+      float scale, rb = 0.0f;
+      if (a.bfp) {
+        if (lane == leader) e = bfp_exponent(bm);
+        e = __shfl_sync(0xffffffffu, e, leader);
+        scale = pow2f(e + 2 - a.bits);
+      } else {
+        scale = bm / qmax;
+        if (bm >= 0x1p-60f && bm < 0x1p126f) rb = __frcp_rn(bm);
+      }
+      if (!valid) continue;
+      if (!have_max && (col & (a.qg1 - 1)) == 0) {
+        a.block_max[blk_row + cb] = bm;
+        if (a.bfp && a.block_exp) a.block_exp[blk_row + cb] = static_cast<float>(e);
+      }
+      if ((col & (a.p - 1)) == 0) a.tile_scale[static_cast<int64_t>(col >> lp) * a.scale_ld + row_idx] = scale;
+      const float inv_p2e = (a.bfp && e <= 126) ? pow2f(-e) : 0.0f;
+      const int q0 = quantize_vec(v[u].x, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      const int q1 = quantize_vec(v[u].y, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      const int q2 = quantize_vec(v[u].z, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      const int q3 = quantize_vec(v[u].w, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      if (a.packed)
+        *reinterpret_cast<uint32_t*>(a.packed + static_cast<int64_t>(row_idx) * kp + col) =
+            static_cast<uint32_t>(q0) | (static_cast<uint32_t>(q1) << 8) | (static_cast<uint32_t>(q2) << 16) |
+            (static_cast<uint32_t>(q3) << 24);
+      store_planes4<KIND, S>(lut, a, static_cast<int64_t>(row_idx) * kp + col, q0, q1, q2, q3);
     }
   }
 }
@@ -313,9 +515,58 @@ static int grid_for(int64_t work_items, int per_block) {
   return static_cast<int>(g);
 }
 
+template <int KIND, int S>
+static void launch_slice_vec_s(const DenseLoader& ld, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
+  slice_dense_vec_kernel<KIND, S><<<grid, 256, 0, stream>>>(ld.x, ld.ld_batch, ld.ld_row, a, have_max);
+}
+
+template <int KIND>
+static void launch_slice_vec_k(const DenseLoader& ld, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
+  switch (a.n_slices) {
+    case 1: launch_slice_vec_s<KIND, 1>(ld, a, grid, have_max, stream); break;
+    case 2: launch_slice_vec_s<KIND, 2>(ld, a, grid, have_max, stream); break;
+    case 3: launch_slice_vec_s<KIND, 3>(ld, a, grid, have_max, stream); break;
+    case 4: launch_slice_vec_s<KIND, 4>(ld, a, grid, have_max, stream); break;
+    case 5: launch_slice_vec_s<KIND, 5>(ld, a, grid, have_max, stream); break;
+    case 6: launch_slice_vec_s<KIND, 6>(ld, a, grid, have_max, stream); break;
+    case 7: launch_slice_vec_s<KIND, 7>(ld, a, grid, have_max, stream); break;
+    default: launch_slice_vec_s<KIND, 8>(ld, a, grid, have_max, stream); break;
+  }
+}
+
+static void launch_slice_vec(const DenseLoader& ld, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
+  if (a.kind == MIB_OPERAND_E4M3)
+    launch_slice_vec_k<MIB_OPERAND_E4M3>(ld, a, grid, have_max, stream);
+  else
+    launch_slice_vec_k<MIB_OPERAND_FP16>(ld, a, grid, have_max, stream);
+}
+
 template <class Loader>
 static cudaError_t launch_slice(const Loader& ld, SliceArgs a, cudaStream_t stream) {
   const bool one_row = (a.qg0 == 1);
+  if constexpr (std::is_same<Loader, DenseLoader>::value) {
+    // vector path: unit column stride, 16-byte aligned rows, unpadded tiles, and a fused max only
+    // when a quant block fits one 128-column chunk
+    auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+    const int64_t groups = ((a.kp + 127) / 128 + kSliceVecChunks - 1) / kSliceVecChunks;
+    const bool vec = ld.ld_col == 1 && (reinterpret_cast<uintptr_t>(ld.x) & 15) == 0 && ld.ld_row % 4 == 0 &&
+                     ld.ld_batch % 4 == 0 && a.cols % 4 == 0 && a.p == a.pp && a.p >= 4 && pow2(a.p) &&
+                     pow2(a.qg1) && a.kp == a.row_pitch && a.kp < (int64_t{1} << 30) &&
+                     a.batch * a.rows * groups < (int64_t{1} << 30) && (!one_row || a.qg1 <= 128);
+    if (vec) {
+      if (!one_row) {
+        block_absmax_kernel<<<grid_for(a.batch * a.nbr * a.nbc, 8), 256, 0, stream>>>(
+            ld, a.batch, a.rows, a.cols, a.qg0, a.qg1, a.nbr, a.nbc, a.block_max);
+        count_launch();
+      }
+      int64_t g = (a.batch * a.rows * groups + 7) / 8;
+      g = g < 1 ? 1 : (g > 148 * 4 ? 148 * 4 : g);
+      launch_slice_vec(ld, a, static_cast<int>(g), !one_row, stream);
+      count_launch();
+      if (!one_row && a.bfp && a.block_exp) launch_block_exp(a.block_max, a.block_exp, a.batch * a.nbr * a.nbc, stream);
+      return cudaGetLastError();
+    }
+  }
   if (!one_row) {
     block_absmax_kernel<<<grid_for(a.batch * a.nbr * a.nbc, 8), 256, 0, stream>>>(ld, a.batch, a.rows, a.cols, a.qg0,
                                                                                    a.qg1, a.nbr, a.nbc, a.block_max);

@@ -121,3 +121,49 @@ def test_split_k_matches_single_pass(name, cuda):
     assert rel_norm(a, b) < 1e-6
     oxs, ows, oeng, wl = oracle_pair(c)
     assert rel_norm(a, O.mvm_exact(oxs, ows, oeng, wl)) <= 1e-5
+
+
+def _boundary_matrix(rng, rows, cols, block, bits, bfp):
+    """Values on and within 3 ulp of the quantisation rounding boundaries of every row block.
+
+    INT: (k + 1/2) / (2^(bits-1) - 1) * bmax; BFP: (k + 1/2) * 2^(e + 2 - bits).  Block maxima span
+    2^-50 .. 2^60, and each block holds its maximum exactly once.
+    """
+    qmax = (1 << (bits - 1)) - 1
+    x = np.empty((rows, cols), np.float32)
+    for r in range(rows):
+        for c0 in range(0, cols, block):
+            n = min(block, cols - c0)
+            bm = np.float32(np.ldexp(1.0 + rng.random(), int(rng.integers(-50, 60))))
+            if bfp:
+                e = int(O.bfp_exponent(np.array([bm], np.float32))[0])
+                k = rng.integers(-(qmax + 1), qmax, n).astype(np.float64)
+                t = ((k + 0.5) * np.ldexp(1.0, e + 2 - bits)).astype(np.float32)
+            else:
+                k = rng.integers(-qmax, qmax, n).astype(np.float64)
+                t = (np.float32(1.0) * ((2 * k + 1) / (2 * qmax)).astype(np.float32) * bm).astype(np.float32)
+            d = rng.integers(-3, 4, n).astype(np.int32)
+            v = (t.view(np.int32) + d).view(np.float32)
+            v = np.clip(v, -bm, bm).astype(np.float32)
+            v[int(rng.integers(0, n))] = bm if rng.random() < 0.5 else -bm
+            x[r, c0:c0 + n] = v
+    return x
+
+
+@pytest.mark.parametrize("bfp,gran", [(False, (1, 128)), (False, (1, 64)), (False, (4, 128)),
+                                      (True, (1, 128)), (True, (1, 256)), (False, (1, 256))])
+def test_slice_rounding_boundaries(bfp, gran, cuda):
+    """Codes of values placed on the INT/BFP rounding boundaries equal the oracle's bit for bit
+    (fp32 division and round-half-even as data_formats.py:116-207 computes them)."""
+    import memintelli_flash_b200 as M
+    rng = np.random.default_rng(7 + gran[0] + gran[1] + int(bfp))
+    sm = [1, 1, 2, 2, 2]
+    x = _boundary_matrix(rng, 64, 1024, gran[1], sum(sm), bfp)
+    eng = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0,
+                      rate_stuck_LGS=0.0, read_variation=0.0, vnoise=0.0, rdac=4, g_level=4, radc=4096)
+    xs = M.SlicedData(torch.tensor(sm), bw_e=8 if bfp else None, is_weight=False, paral_size=(1, 32),
+                      quant_gran=gran, device=cuda, inference=False)
+    xs.slice_data_imp(eng, torch.from_numpy(x).to(cuda))
+    ref = O.slice_matrix(x, sm, bw_e=8 if bfp else None, paral_size=(1, 32), quant_gran=gran)
+    assert np.array_equal(xs._buf["block_max"].cpu().numpy().reshape(ref.bmax.shape), ref.bmax)
+    assert np.array_equal(xs.sliced_data.cpu().numpy(), ref.sliced_data())
