@@ -273,9 +273,71 @@ __device__ __forceinline__ int quantize_vec(float v, float bmax, float rb, float
   return q & ((1 << bits) - 1);
 }
 
-template <int KIND, int S>
-__global__ void __launch_bounds__(256, 4) slice_dense_vec_kernel(const float* __restrict__ x, int64_t ld_batch,
-                                                                 int64_t ld_row, SliceArgs a, bool have_max) {
+// Element sources of the vector kernel.  row(b, r) prepares a per-row context once per work item;
+// load4(row, col) returns columns col..col+3 of that row, zero beyond the matrix.
+
+// Dense rows: unit column stride, 16-byte aligned rows, cols % 4 == 0 (one float4 per call).
+struct DenseRowSrc {
+  const float* x;
+  int64_t ld_batch, ld_row;
+  int cols;
+  struct Row {
+    const float* p;
+  };
+  __device__ __forceinline__ Row row(int b, int r) const {
+    return {x + b * ld_batch + static_cast<int64_t>(r) * ld_row};
+  }
+  __device__ __forceinline__ float4 load4(const Row& w, int col) const {
+    return col < cols ? __ldg(reinterpret_cast<const float4*>(w.p + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+};
+
+// Convolution patches in F.unfold order: column c = ci*kh*kw + i*kw + j of output pixel r = oh*Wo + ow
+// of image b reads x[b, ci, oh*sh - ph + i*dh, ow*sw - pw + j*dw] (zero outside the image).  One
+// image holds fewer than 2^31 elements.  KH > 0 fixes a square KH x KH kernel at compile time, so the
+// column decomposition is a multiply-shift; the next three columns follow by incrementing (ci, i, j).
+template <int KH>
+struct ConvRowSrc {
+  const float* x;
+  int C, H, W, Wo, kh, kw, sh, sw, ph, pw, dh, dw, cols;
+  struct Row {
+    const float* p;
+    int ih0, iw0;
+  };
+  __device__ __forceinline__ Row row(int b, int r) const {
+    const int oh = r / Wo, ow = r - (r / Wo) * Wo;
+    return {x + static_cast<int64_t>(b) * C * H * W, oh * sh - ph, ow * sw - pw};
+  }
+  __device__ __forceinline__ float4 load4(const Row& w, int col) const {
+    const unsigned k_h = KH > 0 ? KH : kh, k_w = KH > 0 ? KH : kw;
+    const unsigned c0 = static_cast<unsigned>(col);
+    unsigned ci = c0 / (k_h * k_w);
+    const unsigned rem = c0 - ci * (k_h * k_w);
+    unsigned i = rem / k_w, j = rem - (rem / k_w) * k_w;
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int ih = w.ih0 + static_cast<int>(i) * dh, iw = w.iw0 + static_cast<int>(j) * dw;
+      const bool in = col + u < cols && static_cast<unsigned>(ih) < static_cast<unsigned>(H) &&
+                      static_cast<unsigned>(iw) < static_cast<unsigned>(W);
+      // unsigned: the offset of a column past the end (not loaded) may wrap
+      const unsigned off = (ci * static_cast<unsigned>(H) + static_cast<unsigned>(ih)) * static_cast<unsigned>(W) +
+                           static_cast<unsigned>(iw);
+      v[u] = in ? __ldg(w.p + off) : 0.0f;
+      if (++j == k_w) {
+        j = 0;
+        if (++i == k_h) {
+          i = 0;
+          ++ci;
+        }
+      }
+    }
+    return make_float4(v[0], v[1], v[2], v[3]);
+  }
+};
+
+template <int KIND, int S, class Src>
+__global__ void __launch_bounds__(256, 4) slice_vec_kernel(Src src, SliceArgs a, bool have_max) {
   __shared__ LevelLut<KIND> lut;
   build_level_lut<KIND>(lut, a);
 
@@ -283,7 +345,7 @@ __global__ void __launch_bounds__(256, 4) slice_dense_vec_kernel(const float* __
   const int nwarps = static_cast<int>(gridDim.x * (blockDim.x >> 5));
   const int nrows = static_cast<int>(a.batch * a.rows);
   const int rows = static_cast<int>(a.rows);
-  const int kp = static_cast<int>(a.kp), cols = static_cast<int>(a.cols);
+  const int kp = static_cast<int>(a.kp);
   const int nchunks = (kp + 127) / 128;
   const int ngroups = (nchunks + kSliceVecChunks - 1) / kSliceVecChunks;
   const int nitems = nrows * ngroups;
@@ -296,13 +358,13 @@ __global__ void __launch_bounds__(256, 4) slice_dense_vec_kernel(const float* __
     const int row_idx = item / ngroups;
     const int ch0 = (item - row_idx * ngroups) * kSliceVecChunks;
     const int b = row_idx / rows, r = row_idx - b * rows;
-    const float* xr = x + b * ld_batch + static_cast<int64_t>(r) * ld_row;
+    const typename Src::Row rw = src.row(b, r);
     const int64_t blk_row = (static_cast<int64_t>(b) * a.nbr + (a.qg0 == 1 ? r : r / a.qg0)) * a.nbc;
     float4 v[kSliceVecChunks];
 #pragma unroll
     for (int u = 0; u < kSliceVecChunks; ++u) {
       const int col = (ch0 + u) * 128 + 4 * lane;
-      v[u] = col < cols ? __ldg(reinterpret_cast<const float4*>(xr + col)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[u] = src.load4(rw, col);
     }
 #pragma unroll
     for (int u = 0; u < kSliceVecChunks; ++u) {
@@ -493,7 +555,7 @@ __global__ void read_noise_kernel(const uint8_t* __restrict__ levels, const floa
           lv = min(max(lv, 0), a.g_level - 1);
           sigma = a.sigma[lv];
         }
-        g[u] = g[u] * expf(z[u] * sigma);
+        g[u] = g[u] * __expf(z[u] * sigma);  // approximate hardware exp: the noise is statistical
       }
     }
     __half2 h0 = __floats2half2_rn((g[0] - a.lgs_f) / a.qg_f, (g[1] - a.lgs_f) / a.qg_f);
@@ -515,56 +577,78 @@ static int grid_for(int64_t work_items, int per_block) {
   return static_cast<int>(g);
 }
 
-template <int KIND, int S>
-static void launch_slice_vec_s(const DenseLoader& ld, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
-  slice_dense_vec_kernel<KIND, S><<<grid, 256, 0, stream>>>(ld.x, ld.ld_batch, ld.ld_row, a, have_max);
-}
-
-template <int KIND>
-static void launch_slice_vec_k(const DenseLoader& ld, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
+template <int KIND, class Src>
+static void launch_slice_vec_k(const Src& src, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
   switch (a.n_slices) {
-    case 1: launch_slice_vec_s<KIND, 1>(ld, a, grid, have_max, stream); break;
-    case 2: launch_slice_vec_s<KIND, 2>(ld, a, grid, have_max, stream); break;
-    case 3: launch_slice_vec_s<KIND, 3>(ld, a, grid, have_max, stream); break;
-    case 4: launch_slice_vec_s<KIND, 4>(ld, a, grid, have_max, stream); break;
-    case 5: launch_slice_vec_s<KIND, 5>(ld, a, grid, have_max, stream); break;
-    case 6: launch_slice_vec_s<KIND, 6>(ld, a, grid, have_max, stream); break;
-    case 7: launch_slice_vec_s<KIND, 7>(ld, a, grid, have_max, stream); break;
-    default: launch_slice_vec_s<KIND, 8>(ld, a, grid, have_max, stream); break;
+    case 1: slice_vec_kernel<KIND, 1, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    case 2: slice_vec_kernel<KIND, 2, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    case 3: slice_vec_kernel<KIND, 3, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    case 4: slice_vec_kernel<KIND, 4, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    case 5: slice_vec_kernel<KIND, 5, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    case 6: slice_vec_kernel<KIND, 6, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    case 7: slice_vec_kernel<KIND, 7, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
+    default: slice_vec_kernel<KIND, 8, Src><<<grid, 256, 0, stream>>>(src, a, have_max); break;
   }
 }
 
-static void launch_slice_vec(const DenseLoader& ld, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
+template <class Src>
+static void launch_slice_vec(const Src& src, const SliceArgs& a, int grid, bool have_max, cudaStream_t stream) {
   if (a.kind == MIB_OPERAND_E4M3)
-    launch_slice_vec_k<MIB_OPERAND_E4M3>(ld, a, grid, have_max, stream);
+    launch_slice_vec_k<MIB_OPERAND_E4M3>(src, a, grid, have_max, stream);
   else
-    launch_slice_vec_k<MIB_OPERAND_FP16>(ld, a, grid, have_max, stream);
+    launch_slice_vec_k<MIB_OPERAND_FP16>(src, a, grid, have_max, stream);
+}
+
+// The vector kernel needs unpadded power-of-two tiles and power-of-two quant blocks, index ranges that
+// fit 32-bit arithmetic, and a fused max only when a quant block fits one 128-column chunk.
+static bool slice_vec_eligible(const SliceArgs& a) {
+  auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
+  const int64_t groups = ((a.kp + 127) / 128 + kSliceVecChunks - 1) / kSliceVecChunks;
+  return a.p == a.pp && a.p >= 4 && pow2(a.p) && pow2(a.qg1) && a.kp == a.row_pitch &&
+         a.kp < (int64_t{1} << 30) && a.batch * a.rows * groups < (int64_t{1} << 30) &&
+         (a.qg0 != 1 || a.qg1 <= 128);
+}
+
+template <class Loader, class Src>
+static cudaError_t launch_slice_vec_path(const Loader& ld, const Src& src, SliceArgs a, cudaStream_t stream) {
+  const bool one_row = (a.qg0 == 1);
+  if (!one_row) {
+    block_absmax_kernel<<<grid_for(a.batch * a.nbr * a.nbc, 8), 256, 0, stream>>>(ld, a.batch, a.rows, a.cols, a.qg0,
+                                                                                   a.qg1, a.nbr, a.nbc, a.block_max);
+    count_launch();
+  }
+  const int64_t groups = ((a.kp + 127) / 128 + kSliceVecChunks - 1) / kSliceVecChunks;
+  int64_t g = (a.batch * a.rows * groups + 7) / 8;
+  g = g < 1 ? 1 : (g > 148 * 4 ? 148 * 4 : g);
+  launch_slice_vec(src, a, static_cast<int>(g), !one_row, stream);
+  count_launch();
+  if (!one_row && a.bfp && a.block_exp) launch_block_exp(a.block_max, a.block_exp, a.batch * a.nbr * a.nbc, stream);
+  return cudaGetLastError();
 }
 
 template <class Loader>
 static cudaError_t launch_slice(const Loader& ld, SliceArgs a, cudaStream_t stream) {
   const bool one_row = (a.qg0 == 1);
   if constexpr (std::is_same<Loader, DenseLoader>::value) {
-    // vector path: unit column stride, 16-byte aligned rows, unpadded tiles, and a fused max only
-    // when a quant block fits one 128-column chunk
-    auto pow2 = [](int64_t v) { return v > 0 && (v & (v - 1)) == 0; };
-    const int64_t groups = ((a.kp + 127) / 128 + kSliceVecChunks - 1) / kSliceVecChunks;
-    const bool vec = ld.ld_col == 1 && (reinterpret_cast<uintptr_t>(ld.x) & 15) == 0 && ld.ld_row % 4 == 0 &&
-                     ld.ld_batch % 4 == 0 && a.cols % 4 == 0 && a.p == a.pp && a.p >= 4 && pow2(a.p) &&
-                     pow2(a.qg1) && a.kp == a.row_pitch && a.kp < (int64_t{1} << 30) &&
-                     a.batch * a.rows * groups < (int64_t{1} << 30) && (!one_row || a.qg1 <= 128);
-    if (vec) {
-      if (!one_row) {
-        block_absmax_kernel<<<grid_for(a.batch * a.nbr * a.nbc, 8), 256, 0, stream>>>(
-            ld, a.batch, a.rows, a.cols, a.qg0, a.qg1, a.nbr, a.nbc, a.block_max);
-        count_launch();
-      }
-      int64_t g = (a.batch * a.rows * groups + 7) / 8;
-      g = g < 1 ? 1 : (g > 148 * 4 ? 148 * 4 : g);
-      launch_slice_vec(ld, a, static_cast<int>(g), !one_row, stream);
-      count_launch();
-      if (!one_row && a.bfp && a.block_exp) launch_block_exp(a.block_max, a.block_exp, a.batch * a.nbr * a.nbc, stream);
-      return cudaGetLastError();
+    // dense rows: unit column stride and 16-byte aligned rows for the float4 loads
+    if (slice_vec_eligible(a) && ld.ld_col == 1 && (reinterpret_cast<uintptr_t>(ld.x) & 15) == 0 &&
+        ld.ld_row % 4 == 0 && ld.ld_batch % 4 == 0 && a.cols % 4 == 0)
+      return launch_slice_vec_path(ld, DenseRowSrc{ld.x, ld.ld_batch, ld.ld_row, static_cast<int>(a.cols)}, a,
+                                   stream);
+  } else {
+    // convolution patches: one image in 32-bit indexing
+    if (slice_vec_eligible(a) && ld.C * ld.H * ld.W < (int64_t{1} << 31) && ld.Wo > 0) {
+      auto conv_src = [&](auto kh) {
+        using Src = ConvRowSrc<decltype(kh)::value>;
+        return Src{ld.x, static_cast<int>(ld.C), static_cast<int>(ld.H), static_cast<int>(ld.W),
+                   static_cast<int>(ld.Wo), ld.kh, ld.kw, ld.sh, ld.sw, ld.ph, ld.pw, ld.dh, ld.dw,
+                   static_cast<int>(a.cols)};
+      };
+      if (ld.kh == 3 && ld.kw == 3)
+        return launch_slice_vec_path(ld, conv_src(std::integral_constant<int, 3>{}), a, stream);
+      if (ld.kh == 1 && ld.kw == 1)
+        return launch_slice_vec_path(ld, conv_src(std::integral_constant<int, 1>{}), a, stream);
+      return launch_slice_vec_path(ld, conv_src(std::integral_constant<int, 0>{}), a, stream);
     }
   }
   if (!one_row) {

@@ -67,26 +67,60 @@ class SlicedData(object):
         self.inference = inference
         self.paral_size = paral_size
         self.quant_gran = paral_size if quant_gran is None else quant_gran
-        if slice_method[0] != 1:
+        sm = slice_method.tolist() if torch.is_tensor(slice_method) else [int(v) for v in slice_method]
+        if sm[0] != 1:
             raise ValueError('The first bit of the slice method should be 1')
         self.slice_method = slice_method
         self._overrides = {}
         self._cache = {}
         self._buf = None
-        self._init_data(slice_method, device)
+        self._init_data(sm, device)
+        self._sm_src = slice_method
 
     def _init_data(self, slice_method, device):
-        """Per-slice max code and shift weight, LSB-first (data_formats.py:60-71)."""
-        assert slice_method[0] == 1, 'the first slice should be 1'
-        sm = [int(s) for s in slice_method]
-        self.sliced_max_weights = torch.zeros(len(sm), device=device)
-        self.sliced_weights = torch.zeros(len(sm), device=device)
-        temp_s = 0
-        for i, s in enumerate(sm[::-1]):
-            self.sliced_max_weights[i] = 2 ** s - 1
-            self.sliced_weights[i] = 2 ** temp_s
+        """Per-slice max code and shift weight, LSB-first (data_formats.py:60-71).
+
+        The values are kept on the host; ``sliced_max_weights`` / ``sliced_weights`` become
+        float32 tensors on ``device`` on first access, so building a SlicedData launches
+        nothing and the MVM checks read host values without a device round trip.
+        """
+        sm = slice_method.tolist() if torch.is_tensor(slice_method) else [int(v) for v in slice_method]
+        assert sm[0] == 1, 'the first slice should be 1'
+        self._sm_list, self._sm_src = sm, slice_method
+        self._max_host = [float(2 ** s - 1) for s in sm[::-1]]
+        w, temp_s = [], 0
+        for s in sm[::-1]:
+            w.append(float(2 ** temp_s))
             temp_s += s
-        self.sliced_weights[-1] *= -1
+        w[-1] = -w[-1]
+        self._weights_host = w
+        self._max_t = None
+        self._weights_t = None
+
+    def _host_tensor(self, attr, values):
+        t = getattr(self, attr)
+        if t is None:
+            t = torch.tensor(values, dtype=torch.float32, device=self.device)
+            setattr(self, attr, t)
+        return t
+
+    sliced_max_weights = property(lambda self: self._host_tensor("_max_t", self._max_host),
+                                  lambda self, v: setattr(self, "_max_t", v))
+    sliced_weights = property(lambda self: self._host_tensor("_weights_t", self._weights_host),
+                              lambda self, v: setattr(self, "_weights_t", v))
+
+    def _max_codes(self):
+        """Per-slice max codes as host floats (a tensor assigned to ``sliced_max_weights`` wins)."""
+        if self._max_t is not None:
+            return [float(v) for v in self._max_t.tolist()]
+        return self._max_host
+
+    def _slices(self):
+        """The slice method as a host list of ints (read from ``slice_method`` once per object)."""
+        if getattr(self, "_sm_src", None) is not self.slice_method:
+            self._sm_list = [int(s) for s in self.slice_method]
+            self._sm_src = self.slice_method
+        return self._sm_list
 
     def __repr__(self):
         return 'sliced data with slice_method:{}'.format(self.slice_method)
@@ -97,7 +131,7 @@ class SlicedData(object):
     # ------------------------------------------------------------------ helpers
     def _spec(self) -> N.SliceSpec:
         g = self._buf["geom"]
-        sm = [int(s) for s in self.slice_method]
+        sm = self._slices()
         sp = N.SliceSpec()
         sp.n_slices = len(sm)
         for i, s in enumerate(sm):
@@ -115,7 +149,7 @@ class SlicedData(object):
 
     @property
     def bits(self):
-        return int(sum(int(s) for s in self.slice_method))
+        return int(sum(self._slices()))
 
     # ------------------------------------------------------------ slicing
     def slice_data_imp(self, engine, data):
@@ -195,7 +229,7 @@ class SlicedData(object):
         q = self._padded_codes()
         if q is None:
             return None
-        sm = [int(s) for s in self.slice_method]
+        sm = self._slices()
         planes = []
         off = 0
         for w in sm[::-1]:

@@ -273,7 +273,7 @@ class DPETensor(object):
         gx, gw = x._buf["geom"], mat._buf["geom"]
         if gx["kp"] != gw["kp"] or gx["p"] != gw["p"] or x._buf["kind"] != mat._buf["kind"]:
             raise ValueError('The input data mismatches the shape of weight data!')
-        if max(float(v) for v in mat.sliced_max_weights) > self.g_level - 1:
+        if max(mat._max_codes()) > self.g_level - 1:
             raise ValueError('The weight data is out of the range!')
         dev = x._buf["planes"].device
         M = gx["batch"] * gx["rows"]

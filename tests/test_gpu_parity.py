@@ -167,3 +167,25 @@ def test_slice_rounding_boundaries(bfp, gran, cuda):
     ref = O.slice_matrix(x, sm, bw_e=8 if bfp else None, paral_size=(1, 32), quant_gran=gran)
     assert np.array_equal(xs._buf["block_max"].cpu().numpy().reshape(ref.bmax.shape), ref.bmax)
     assert np.array_equal(xs.sliced_data.cpu().numpy(), ref.sliced_data())
+
+
+@pytest.mark.parametrize("k,s,p,d,bfp,gran", [(3, 1, 1, 1, False, (1, 64)), (3, 2, 0, 1, True, (1, 64)),
+                                              (1, 2, 0, 1, False, (1, 128)), (5, 1, 2, 2, True, (1, 64)),
+                                              (2, 1, 0, 1, False, (1, 32)), (3, 1, 1, 1, False, (4, 64))])
+def test_conv_patch_slicing(k, s, p, d, bfp, gran, cuda):
+    """Codes and block maxima of convolution patches equal the oracle's on F.unfold of the same input
+    (convolution.py:111-137 unfolds, then data_formats.py:116-207 slices)."""
+    import memintelli_flash_b200 as M
+    g = torch.Generator().manual_seed(11 + k + s + p + d)
+    x = torch.randn(2, 5, 11, 13, generator=g)
+    sm = [1, 1, 2, 2, 2]
+    eng = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0,
+                      rate_stuck_LGS=0.0, read_variation=0.0, vnoise=0.0, rdac=4, g_level=4, radc=4096)
+    sd = M.SlicedData(torch.tensor(sm), bw_e=8 if bfp else None, is_weight=False, paral_size=(1, 32),
+                      quant_gran=gran, device=cuda, inference=False)
+    sd._slice_conv_imp(eng, x.to(cuda), (k, k), (s, s), (p, p), (d, d))
+    cols = torch.nn.functional.unfold(x, k, dilation=d, padding=p, stride=s)      # (N, C*k*k, L)
+    ref = O.slice_matrix(cols.transpose(1, 2).contiguous().numpy(), sm, bw_e=8 if bfp else None,
+                         paral_size=(1, 32), quant_gran=gran)
+    assert np.array_equal(sd._buf["block_max"].cpu().numpy().reshape(ref.bmax.shape), ref.bmax)
+    assert np.array_equal(sd.sliced_data.cpu().numpy(), ref.sliced_data())
