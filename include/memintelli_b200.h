@@ -109,6 +109,28 @@ int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_
                          void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
                          cudaStream_t stream);
 
+/* Fused producers of an input (no reference counterpart).  Each slices a row transform of x with
+ * the same arguments and buffers as mib_slice_input, without materialising the transformed matrix;
+ * in the reference they are a torch pass followed by SlicedData.slice_data_imp.  Both need one-row
+ * input quant blocks (quant_gran[0] == 1), unpadded power-of-two tiles, power-of-two quant blocks
+ * of at most 128 columns, cols % 4 == 0 and 16-byte aligned rows; otherwise they return
+ * MIB_ERR_UNSUPPORTED and the caller runs the transform and mib_slice_input.
+ *
+ * mib_slice_rmsnorm_input: row-wise RMSNorm, y = x * rsqrt(mean(x^2) + eps) * norm_weight
+ * (norm_weight: cols floats, 16-byte aligned).  The sum of squares is a warp reduction, so y can
+ * differ from torch's in the last fp32 bit. */
+int mib_slice_rmsnorm_input(const float* x, int64_t batch, int64_t rows, int64_t cols, int64_t ld_batch,
+                            int64_t ld_row, const float* norm_weight, float eps, const mib_slice_spec* spec,
+                            const mib_k_geom* kg, int32_t rdac, int32_t operand_kind, void* planes, float* tile_scale,
+                            float* block_max, float* block_exp, uint8_t* packed, cudaStream_t stream);
+
+/* mib_slice_swiglu_input: SwiGLU of a fused gate/up activation, y[c] = silu(x[c]) * x[up_offset + c]
+ * for c < cols (silu(g) = g / (1 + exp(-g))); up_offset % 4 == 0. */
+int mib_slice_swiglu_input(const float* gate_up, int64_t batch, int64_t rows, int64_t cols, int64_t ld_batch,
+                           int64_t ld_row, int64_t up_offset, const mib_slice_spec* spec, const mib_k_geom* kg,
+                           int32_t rdac, int32_t operand_kind, void* planes, float* tile_scale, float* block_max,
+                           float* block_exp, uint8_t* packed, cudaStream_t stream);
+
 /* Quantise, slice and program a weight matrix W (K, N) into conductance-level planes.
  * Replaces SlicedData.slice_data_imp for weights + DPETensor._num2G (memmat_tensor.py:160-202):
  * level = round(code/m*(g-1)); stuck-at faults from `stuck_field` (torch.rand with the

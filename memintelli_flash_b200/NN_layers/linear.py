@@ -51,6 +51,18 @@ class LinearMem(nn.Module):
         input_sliced.slice_data_imp(self.engine, input.detach())
         return linear_mem_func(self.engine, input, self.weight, input_sliced, self.weight_sliced, self.bias)
 
+    def new_input(self):
+        """An empty input SlicedData with this layer's input slicing, for the engine's fused
+        producers (``DPETensor.slice_rmsnorm_input`` / ``slice_swiglu_input``)."""
+        return SlicedData(self.input_slice_method, device=self.engine.device, bw_e=self.weight_sliced.bw_e,
+                          is_weight=False, paral_size=self.input_paral_size, quant_gran=self.input_quant_gran,
+                          inference=True)
+
+    def forward_sliced(self, input_sliced) -> torch.Tensor:
+        """Inference forward of an input already sliced (by ``new_input`` + a fused producer)."""
+        bias = None if self.bias is None else self.bias.detach().float()
+        return self.engine.MapReduceDot(input_sliced, self.weight_sliced, bias=bias)
+
     def _forward_inference(self, input: torch.Tensor) -> torch.Tensor:
         """Inference forward: the bias add is fused into the kernel's output store."""
         input_sliced = self._input_sliced(input, True)

@@ -79,6 +79,14 @@ class _ShardBase(torch.nn.Module):
         self.local.inference_mode = True
         self.local.weight_sliced.inference = True
 
+    def new_input(self):
+        """An empty input SlicedData for this rank's crossbars (see ``LinearMem.new_input``)."""
+        return self.local.new_input()
+
+    def forward_sliced(self, input_sliced):
+        """``forward`` for an input already sliced by a fused producer."""
+        return self._finish(self.local.forward_sliced(input_sliced))
+
 
 class _LinearFromWeight(LinearMem):
     """LinearMem programmed from a given weight (no random init, programmed once)."""
@@ -153,7 +161,9 @@ class ColumnShardedLinearMem(_ShardBase):
         return self._fused_sizes
 
     def forward(self, x):
-        y = self.local(x)
+        return self._finish(self.local(x))
+
+    def _finish(self, y):
         if not self.gather or self.world == 1:
             return y
         width = max(self.shard_sizes)
@@ -172,7 +182,9 @@ class RowShardedLinearMem(_ShardBase):
         super().__init__(engine, weight, bias, 1, input_slice, weight_slice, **kw)
 
     def forward(self, x_local):
-        y = self.local(x_local)
+        return self._finish(self.local(x_local))
+
+    def _finish(self, y):
         if self.world > 1:
             dist.all_reduce(y, group=self.group)
         if self.full_bias is not None:

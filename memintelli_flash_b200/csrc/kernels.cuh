@@ -91,6 +91,10 @@ struct MvmArgs {
 };
 
 cudaError_t slice_dense(const float* x, int64_t ld_batch, int64_t ld_row, SliceArgs a, cudaStream_t stream);
+cudaError_t slice_rmsnorm(const float* x, int64_t ld_batch, int64_t ld_row, const float* w, float eps, SliceArgs a,
+                          cudaStream_t stream);
+cudaError_t slice_swiglu(const float* x, int64_t ld_batch, int64_t ld_row, int64_t up_offset, SliceArgs a,
+                         cudaStream_t stream);
 cudaError_t slice_conv(const float* x, int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo, int kh, int kw, int sh,
                        int sw, int ph, int pw, int dh, int dw, SliceArgs a, cudaStream_t stream);
 cudaError_t program_weight(const float* w, int64_t stride_k, int64_t stride_n, ProgramArgs a, cudaStream_t stream);

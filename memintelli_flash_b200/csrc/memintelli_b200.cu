@@ -328,6 +328,51 @@ int mib_slice_input(const float* x, int64_t batch, int64_t rows, int64_t cols, i
   return MIB_OK;
 }
 
+// Shared checks of the fused producers; fills `a` on success.
+static int fused_input_args(mib::SliceArgs& a, const float* x, int64_t batch, int64_t rows, int64_t cols,
+                            const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                            void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed) {
+  SliceTab t;
+  if (int r = make_tab(spec, t)) return r;
+  if (!x) return fail(MIB_ERR_PARAM, "input is NULL");
+  if (batch < 1 || rows < 1 || cols < 1) return fail(MIB_ERR_SHAPE, "input must be non-empty");
+  if (int r = check_input_geom(t, spec, kg, cols, rdac, operand_kind, planes, tile_scale, block_max)) return r;
+  if (spec->bfp && !block_exp) return fail(MIB_ERR_PARAM, "block floating point needs the exponent buffer");
+  fill_slice_args(a, t, spec, kg, batch, rows, cols, rdac, operand_kind, planes, tile_scale, block_max, block_exp,
+                  packed);
+  return MIB_OK;
+}
+
+int mib_slice_rmsnorm_input(const float* x, int64_t batch, int64_t rows, int64_t cols, int64_t ld_batch,
+                            int64_t ld_row, const float* norm_weight, float eps, const mib_slice_spec* spec,
+                            const mib_k_geom* kg, int32_t rdac, int32_t operand_kind, void* planes, float* tile_scale,
+                            float* block_max, float* block_exp, uint8_t* packed, cudaStream_t stream) {
+  mib::SliceArgs a;
+  if (int r = fused_input_args(a, x, batch, rows, cols, spec, kg, rdac, operand_kind, planes, tile_scale, block_max,
+                               block_exp, packed))
+    return r;
+  if (!norm_weight) return fail(MIB_ERR_PARAM, "norm weight is NULL");
+  cudaError_t e = mib::slice_rmsnorm(x, ld_batch, ld_row, norm_weight, eps, a, stream);
+  if (e == cudaErrorNotSupported) return fail(MIB_ERR_UNSUPPORTED, "layout not supported by the fused RMSNorm slicing");
+  if (e != cudaSuccess) return cuda_fail(e, "slice_rmsnorm_input launch");
+  return MIB_OK;
+}
+
+int mib_slice_swiglu_input(const float* gate_up, int64_t batch, int64_t rows, int64_t cols, int64_t ld_batch,
+                           int64_t ld_row, int64_t up_offset, const mib_slice_spec* spec, const mib_k_geom* kg,
+                           int32_t rdac, int32_t operand_kind, void* planes, float* tile_scale, float* block_max,
+                           float* block_exp, uint8_t* packed, cudaStream_t stream) {
+  mib::SliceArgs a;
+  if (int r = fused_input_args(a, gate_up, batch, rows, cols, spec, kg, rdac, operand_kind, planes, tile_scale,
+                               block_max, block_exp, packed))
+    return r;
+  if (up_offset < cols) return fail(MIB_ERR_SHAPE, "up columns overlap the gate columns");
+  cudaError_t e = mib::slice_swiglu(gate_up, ld_batch, ld_row, up_offset, a, stream);
+  if (e == cudaErrorNotSupported) return fail(MIB_ERR_UNSUPPORTED, "layout not supported by the fused SwiGLU slicing");
+  if (e != cudaSuccess) return cuda_fail(e, "slice_swiglu_input launch");
+  return MIB_OK;
+}
+
 int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
                          int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
                          const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,

@@ -336,6 +336,63 @@ struct ConvRowSrc {
   }
 };
 
+// Fused producers (no reference counterpart: they replace a torch pass before the slicing).
+
+// RMSNorm of each row, y = x * rsqrt(mean(x^2) + eps) * w, evaluated in that order.  row() is
+// warp-collective: the warp reduces the row's sum of squares (cols % 4 == 0, 16-byte aligned rows).
+struct RmsNormRowSrc {
+  const float* x;
+  const float* w;
+  int64_t ld_batch, ld_row;
+  int cols;
+  float eps;
+  struct Row {
+    const float* p;
+    float rstd;
+  };
+  __device__ __forceinline__ Row row(int b, int r) const {
+    const float* p = x + b * ld_batch + static_cast<int64_t>(r) * ld_row;
+    float ss = 0.0f;
+    for (int c = 4 * (threadIdx.x & 31); c < cols; c += 128) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(p + c));
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    return {p, rsqrtf(ss / static_cast<float>(cols) + eps)};
+  }
+  __device__ __forceinline__ float4 load4(const Row& rw, int col) const {
+    if (col >= cols) return make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 v = __ldg(reinterpret_cast<const float4*>(rw.p + col));
+    const float4 g = __ldg(reinterpret_cast<const float4*>(w + col));
+    return make_float4(v.x * rw.rstd * g.x, v.y * rw.rstd * g.y, v.z * rw.rstd * g.z, v.w * rw.rstd * g.w);
+  }
+};
+
+// SwiGLU of a fused gate/up row, y[c] = silu(gate[c]) * up[c] with silu(g) = g / (1 + exp(-g)); gate
+// columns start at 0 and up columns at up_offset of the same row (cols and up_offset % 4 == 0).
+struct SwigluRowSrc {
+  const float* x;
+  int64_t ld_batch, ld_row, up_offset;
+  int cols;
+  struct Row {
+    const float* p;
+  };
+  __device__ __forceinline__ Row row(int b, int r) const {
+    return {x + b * ld_batch + static_cast<int64_t>(r) * ld_row};
+  }
+  __device__ __forceinline__ static float swish(float g, float u) { return g / (1.0f + expf(-g)) * u; }
+  __device__ __forceinline__ float4 load4(const Row& rw, int col) const {
+    if (col >= cols) return make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 g = __ldg(reinterpret_cast<const float4*>(rw.p + col));
+    const float4 u = __ldg(reinterpret_cast<const float4*>(rw.p + up_offset + col));
+    return make_float4(swish(g.x, u.x), swish(g.y, u.y), swish(g.z, u.z), swish(g.w, u.w));
+  }
+};
+
 template <int KIND, int S, class Src>
 __global__ void __launch_bounds__(256, 4) slice_vec_kernel(Src src, SliceArgs a, bool have_max) {
   __shared__ LevelLut<KIND> lut;
@@ -680,6 +737,28 @@ void launch_block_exp(const float* bmax, float* bexp, int64_t n, cudaStream_t st
 cudaError_t slice_dense(const float* x, int64_t ld_batch, int64_t ld_row, SliceArgs a, cudaStream_t stream) {
   DenseLoader ld{x, ld_batch, ld_row, 1, a.rows, a.cols};
   return launch_slice(ld, a, stream);
+}
+
+// Fused producers: only the vector path (16-byte aligned rows, cols % 4 == 0, one-row quant blocks).
+static bool fused_eligible(const void* x, int64_t ld_batch, int64_t ld_row, const SliceArgs& a) {
+  return slice_vec_eligible(a) && a.qg0 == 1 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && ld_row % 4 == 0 &&
+         ld_batch % 4 == 0 && a.cols % 4 == 0;
+}
+
+cudaError_t slice_rmsnorm(const float* x, int64_t ld_batch, int64_t ld_row, const float* w, float eps, SliceArgs a,
+                          cudaStream_t stream) {
+  if (!fused_eligible(x, ld_batch, ld_row, a) || (reinterpret_cast<uintptr_t>(w) & 15) != 0)
+    return cudaErrorNotSupported;
+  DenseLoader ld{x, ld_batch, ld_row, 1, a.rows, a.cols};
+  return launch_slice_vec_path(ld, RmsNormRowSrc{x, w, ld_batch, ld_row, static_cast<int>(a.cols), eps}, a, stream);
+}
+
+cudaError_t slice_swiglu(const float* x, int64_t ld_batch, int64_t ld_row, int64_t up_offset, SliceArgs a,
+                         cudaStream_t stream) {
+  if (!fused_eligible(x, ld_batch, ld_row, a) || up_offset % 4 != 0) return cudaErrorNotSupported;
+  DenseLoader ld{x, ld_batch, ld_row, 1, a.rows, a.cols};
+  return launch_slice_vec_path(ld, SwigluRowSrc{x, ld_batch, ld_row, up_offset, static_cast<int>(a.cols)}, a,
+                               stream);
 }
 
 cudaError_t slice_conv(const float* x, int64_t C, int64_t H, int64_t W, int64_t Ho, int64_t Wo, int kh, int kw, int sh,

@@ -136,6 +136,14 @@ class DPETensor(object):
         kp = math.ceil(K / qg_k) * qg_k
         return dict(k=K, kp=kp, p=p, pp=padded_tile(p, kind), kt=kp // p)
 
+    def _input_plane_kind(self, kind: int) -> int:
+        """Operand type of input planes.  An engine whose only per-call noise is on the weights
+        (vnoise 0) feeds the MVM FP16 inputs without any noise, so its inputs are sliced straight
+        into FP16 (same tile geometry as E4M3) and the conversion pass is skipped."""
+        if kind == N.OPERAND_E4M3 and self.vnoise == 0 and self.noisy:
+            return N.OPERAND_FP16
+        return kind
+
     def _slice_input(self, sd: SlicedData, data: torch.Tensor):
         squeeze = data.dim() == 2
         x = data.unsqueeze(0) if squeeze else data
@@ -144,10 +152,67 @@ class DPETensor(object):
         B, T, K = x.shape
         qg = _decode_gran(sd.quant_gran, sd.paral_size, T, K)
         kind = self.operand_kind
+        pkind = self._input_plane_kind(kind)
         geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
         self._run_input_slicing(sd, kind, geom, qg, B, T, K, squeeze, lambda spec, kg, bufs: N.call(
-            "mib_slice_input", N.ptr(x), B, T, K, x.stride(0), x.stride(1), spec, kg, int(self.rdac), kind,
-            *bufs, N.stream_ptr(x.device)))
+            "mib_slice_input", N.ptr(x), B, T, K, x.stride(0), x.stride(1), spec, kg, int(self.rdac), pkind,
+            *bufs, N.stream_ptr(x.device)), pkind)
+
+    # ------------------------------------------------------------ fused producers
+    # No reference counterpart: each slices a row transform of an activation without materialising
+    # it (the reference runs the transform in torch, then SlicedData.slice_data_imp).  When the
+    # library does not support the layout, the transform runs in torch and the result is sliced.
+
+    def _slice_fused(self, sd: SlicedData, B: int, T: int, K: int, squeeze: bool, launch, fallback, shape):
+        sd._cache = {}
+        sd._overrides = {}
+        qg = _decode_gran(sd.quant_gran, sd.paral_size, T, K)
+        kind = self.operand_kind
+        pkind = self._input_plane_kind(kind)
+        geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
+        try:
+            self._run_input_slicing(sd, kind, geom, qg, B, T, K, squeeze,
+                                    lambda spec, kg, bufs: launch(spec, kg, pkind, bufs), pkind)
+        except NotImplementedError:
+            self._slice_input(sd, fallback().float())
+        sd.shape = torch.Size(shape)
+
+    @staticmethod
+    def _rows3(x: torch.Tensor):
+        if x.device.type != "cuda":
+            raise RuntimeError("memintelli_flash_b200 computes on CUDA devices only")
+        if x.dtype != torch.float32 or x.dim() not in (2, 3):
+            raise ValueError("fused slicing takes a 2-D or 3-D float32 activation")
+        return (x.unsqueeze(0), True) if x.dim() == 2 else (x, False)
+
+    def slice_rmsnorm_input(self, sd: SlicedData, x: torch.Tensor, weight: torch.Tensor, eps: float):
+        """Slice ``x * rsqrt(mean(x^2, -1) + eps) * weight`` into ``sd`` (an input SlicedData)."""
+        x3, squeeze = self._rows3(x)
+        if x3.stride(-1) != 1:
+            x3 = x3.contiguous()
+        B, T, K = x3.shape
+        w = weight.detach().float().contiguous()
+
+        def fallback():
+            return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+        self._slice_fused(sd, B, T, K, squeeze, lambda spec, kg, pkind, bufs: N.call(
+            "mib_slice_rmsnorm_input", N.ptr(x3), B, T, K, x3.stride(0), x3.stride(1), N.ptr(w), float(eps), spec, kg,
+            int(self.rdac), pkind, *bufs, N.stream_ptr(x3.device)), fallback, x.shape)
+
+    def slice_swiglu_input(self, sd: SlicedData, gate_up: torch.Tensor, width: int):
+        """Slice ``silu(gate_up[..., :width]) * gate_up[..., width:2*width]`` into ``sd``."""
+        x3, squeeze = self._rows3(gate_up)
+        if x3.stride(-1) != 1:
+            x3 = x3.contiguous()
+        B, T, C = x3.shape
+        if C < 2 * width:
+            raise ValueError("gate_up must hold the gate and up columns")
+
+        def fallback():
+            return torch.nn.functional.silu(gate_up[..., :width]) * gate_up[..., width:2 * width]
+        self._slice_fused(sd, B, T, width, squeeze, lambda spec, kg, pkind, bufs: N.call(
+            "mib_slice_swiglu_input", N.ptr(x3), B, T, width, x3.stride(0), x3.stride(1), width, spec, kg,
+            int(self.rdac), pkind, *bufs, N.stream_ptr(x3.device)), fallback, tuple(gate_up.shape[:-1]) + (width,))
 
     def _slice_conv_input(self, sd: SlicedData, x: torch.Tensor, kernel_size, stride, padding, dilation):
         x = x.contiguous()
@@ -161,13 +226,14 @@ class DPETensor(object):
         T, K = ho * wo, c * kh * kw
         qg = _decode_gran(sd.quant_gran, sd.paral_size, T, K)
         kind = self.operand_kind
+        pkind = self._input_plane_kind(kind)
         geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
         self._run_input_slicing(sd, kind, geom, qg, n, T, K, False, lambda spec, kg, bufs: N.call(
             "mib_slice_conv_input", N.ptr(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg,
-            int(self.rdac), kind, *bufs, N.stream_ptr(x.device)))
+            int(self.rdac), pkind, *bufs, N.stream_ptr(x.device)), pkind)
         sd.shape = torch.Size((n, T, K))
 
-    def _run_input_slicing(self, sd, kind, geom, qg, B, T, K, squeeze, launch):
+    def _run_input_slicing(self, sd, kind, geom, qg, B, T, K, squeeze, launch, plane_kind=None):
         dev = self.device
         S = len(sd.slice_method)
         rows = B * T
@@ -175,7 +241,8 @@ class DPETensor(object):
         nbc = math.ceil(K / qg[1])
         geom.update(batch=B, rows=T, squeeze=squeeze, qg=qg, nbr=nbr, nbc=nbc,
                     rows_p=nbr * qg[0], cols_p=nbc * qg[1])
-        pdt = torch.uint8 if kind == N.OPERAND_E4M3 else torch.float16
+        plane_kind = kind if plane_kind is None else plane_kind
+        pdt = torch.uint8 if plane_kind == N.OPERAND_E4M3 else torch.float16
         planes = torch.empty((S, rows, geom["kt"] * geom["pp"]), dtype=pdt, device=dev)
         tile_scale = torch.empty((geom["kt"], rows), dtype=torch.float32, device=dev)
         block_max = torch.empty((B, nbr, nbc), dtype=torch.float32, device=dev)
@@ -288,10 +355,16 @@ class DPETensor(object):
             if kind != N.OPERAND_E4M3:
                 raise NotImplementedError('noisy crossbars with more than 16 DAC / conductance levels')
             seed = int(torch.randint(0, 2 ** 62, (1,)).item())
-            a16 = torch.empty(a_planes.shape, dtype=torch.float16, device=dev)
+            if a_planes.dtype == torch.float16:
+                # sliced straight to FP16 for an engine without voltage noise (_input_plane_kind)
+                if self.vnoise != 0:
+                    raise ValueError('the input was sliced for vnoise=0; slice it again after changing vnoise')
+                a16 = a_planes
+            else:
+                a16 = torch.empty(a_planes.shape, dtype=torch.float16, device=dev)
+                N.call("mib_input_noise", N.ptr(a_planes), N.ptr(a16), a_planes.numel(), float(self.vnoise), seed,
+                       0, stream)
             b16 = torch.empty(b_planes.shape, dtype=torch.float16, device=dev)
-            N.call("mib_input_noise", N.ptr(a_planes), N.ptr(a16), a_planes.numel(), float(self.vnoise), seed, 0,
-                   stream)
             N.call("mib_weight_read_noise", N.ptr(b_planes), N.ptr(mat._buf.get("g_planes")), N.ptr(b16),
                    b_planes.numel(), dspec, seed, 0, stream)
             a_planes, b_planes, kind = a16, b16, N.OPERAND_FP16

@@ -112,12 +112,17 @@ class Qwen3CimLayer(torch.nn.Module):
         if self.local_heads % self.local_kv:
             raise ValueError("each rank's query heads must be a multiple of its key/value heads")
         self.local_inter = self.gate_up_proj.split_sizes[0]
+        self.engine = engine
 
     def forward(self, h, cos, sin):
+        """One decoder layer.  The RMSNorms before the q/k/v and gate/up crossbars and the SwiGLU
+        before the down crossbar run inside the input slicing (``DPETensor.slice_rmsnorm_input`` /
+        ``slice_swiglu_input``), so those activations are never written out."""
         a = self.arch
         B, T, _ = h.shape
-        x = rms_norm(h, self.in_norm, a.eps)
-        qkv = self.qkv_proj(x)
+        xs = self.qkv_proj.new_input()
+        self.engine.slice_rmsnorm_input(xs, h, self.in_norm, a.eps)
+        qkv = self.qkv_proj.forward_sliced(xs)
         nq, nk = self.local_heads * a.head_dim, self.local_kv * a.head_dim
         q = qkv[..., :nq].reshape(B, T, self.local_heads, a.head_dim)
         k = qkv[..., nq:nq + nk].reshape(B, T, self.local_kv, a.head_dim)
@@ -129,10 +134,12 @@ class Qwen3CimLayer(torch.nn.Module):
                                            enable_gqa=self.local_heads != self.local_kv)
         o = o.transpose(1, 2).reshape(B, T, self.local_heads * a.head_dim).float()
         h = h + self.o_proj(o)
-        x = rms_norm(h, self.post_norm, a.eps)
-        gu = self.gate_up_proj(x)
-        m = F.silu(gu[..., :self.local_inter]) * gu[..., self.local_inter:]
-        return h + self.down_proj(m)
+        xs = self.gate_up_proj.new_input()
+        self.engine.slice_rmsnorm_input(xs, h, self.post_norm, a.eps)
+        gu = self.gate_up_proj.forward_sliced(xs)
+        ms = self.down_proj.new_input()
+        self.engine.slice_swiglu_input(ms, gu, self.local_inter)
+        return h + self.down_proj.forward_sliced(ms)
 
 
 class Qwen3CimPrefill(torch.nn.Module):
@@ -142,7 +149,7 @@ class Qwen3CimPrefill(torch.nn.Module):
                  device=None, group=None):
         super().__init__()
         device = device or engine.device
-        self.arch, self.group = arch, group
+        self.arch, self.group, self.engine = arch, group, engine
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         gen = torch.Generator(device=device)
@@ -175,8 +182,9 @@ class Qwen3CimPrefill(torch.nn.Module):
         h = F.embedding(ids, self.embed)
         for layer in self.layers:
             h = layer(h, cos, sin)
-        h = rms_norm(h, self.norm, a.eps)
-        logits = self.lm_head(h[:, :-1])                     # (B, T-1, V_local)
+        xs = self.lm_head.new_input()
+        self.engine.slice_rmsnorm_input(xs, h[:, :-1], self.norm, a.eps)
+        logits = self.lm_head.forward_sliced(xs)             # (B, T-1, V_local)
         target = ids[:, 1:]
         return self._sharded_ce(logits, target)
 
