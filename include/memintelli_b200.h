@@ -211,6 +211,19 @@ int mib_mvm_static_scratch(const void* a_planes, const float* a_scale, int64_t m
                            const int32_t* adc_table, int32_t adc_table_len, float* y, const mib_out_layout* layout,
                            const float* bias, cudaStream_t stream);
 
+/* Attention input preparation for the Qwen3 prefill driver (outside the reference's CIM path, no
+ * reference counterpart).  From the fused q/k/v crossbar output (tokens rows of ld_token floats: q heads,
+ * then k heads, then v heads, head_dim each; token i is position i % seq_len) it writes bf16
+ * q (tokens, q_heads, head_dim), k and v (tokens, kv_heads, head_dim):
+ *   q = rope(rms_norm(q) * q_norm), k = rope(rms_norm(k) * k_norm), v = v,
+ * rms_norm(x) = x * rsqrt(mean(x^2) + eps) and rope(x) = x * cos + rotate_half(x) * sin with
+ * rotate_half(x) = cat(-x[D/2:], x[:D/2]); cos and sin are (seq_len, head_dim) fp32.
+ * head_dim is 64, 128 or 256. */
+int mib_qk_norm_rope_bf16(const float* qkv, int64_t tokens, int64_t ld_token, int32_t seq_len, int32_t q_heads,
+                          int32_t kv_heads, int32_t head_dim, const float* q_norm, const float* k_norm, float eps,
+                          const float* cos_table, const float* sin_table, void* q_out, void* k_out, void* v_out,
+                          cudaStream_t stream);
+
 /* Reads and clears the device-side error flag of the current device (synchronises it).
  * Returns MIB_OK, or MIB_ERR_TIMEOUT when a kernel gave up a bounded wait. */
 int mib_device_status(void);

@@ -56,6 +56,8 @@ _SIGS = {
                                 _P(KGeom), c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     "mib_slice_swiglu_input": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i64, c_i64, _P(SliceSpec), _P(KGeom), c_i32,
                                c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "mib_qk_norm_rope_bf16": [c_vp, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_vp, c_vp, c_f32, c_vp, c_vp, c_vp,
+                              c_vp, c_vp, c_vp],
     "mib_slice_conv_input": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                              _P(SliceSpec), _P(KGeom), c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     "mib_program_weight": [c_vp, c_i64, c_i64, c_i64, c_i64, _P(SliceSpec), _P(KGeom), _P(DeviceSpec), c_vp, c_vp,

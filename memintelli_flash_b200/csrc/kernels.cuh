@@ -103,6 +103,9 @@ cudaError_t input_noise(const uint8_t* in, __half* out, int64_t n, float vnoise,
 cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, int64_t n, ReadNoiseArgs a, uint64_t seed,
                        uint64_t stream_id, cudaStream_t stream);
 void launch_block_exp(const float* bmax, float* bexp, int64_t n, cudaStream_t stream);
+cudaError_t qk_norm_rope(const float* qkv, int64_t tokens, int64_t ld_token, int seq_len, int q_heads, int kv_heads,
+                         int head_dim, const float* q_norm, const float* k_norm, float eps, const float* cos_t,
+                         const float* sin_t, void* q_out, void* k_out, void* v_out, cudaStream_t stream);
 void count_launch(int n = 1);
 size_t mvm_smem_bytes(const MvmArgs& a);
 cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, int64_t N, float* y,

@@ -16,6 +16,7 @@
 
 #include "slice.cu"
 #include "mvm.cu"
+#include "attn_prep.cu"
 
 namespace {
 
@@ -370,6 +371,22 @@ int mib_slice_swiglu_input(const float* gate_up, int64_t batch, int64_t rows, in
   cudaError_t e = mib::slice_swiglu(gate_up, ld_batch, ld_row, up_offset, a, stream);
   if (e == cudaErrorNotSupported) return fail(MIB_ERR_UNSUPPORTED, "layout not supported by the fused SwiGLU slicing");
   if (e != cudaSuccess) return cuda_fail(e, "slice_swiglu_input launch");
+  return MIB_OK;
+}
+
+int mib_qk_norm_rope_bf16(const float* qkv, int64_t tokens, int64_t ld_token, int32_t seq_len, int32_t q_heads,
+                          int32_t kv_heads, int32_t head_dim, const float* q_norm, const float* k_norm, float eps,
+                          const float* cos_table, const float* sin_table, void* q_out, void* k_out, void* v_out,
+                          cudaStream_t stream) {
+  if (!qkv || !q_norm || !k_norm || !cos_table || !sin_table || !q_out || !k_out || !v_out)
+    return fail(MIB_ERR_PARAM, "NULL buffer");
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) return fail(MIB_ERR_UNSUPPORTED, "head_dim must be 64, 128 or 256");
+  if (tokens < 1 || seq_len < 1 || q_heads < 1 || kv_heads < 1) return fail(MIB_ERR_SHAPE, "empty attention input");
+  if (ld_token < static_cast<int64_t>(q_heads + 2 * kv_heads) * head_dim)
+    return fail(MIB_ERR_SHAPE, "ld_token is shorter than the q/k/v heads");
+  cudaError_t e = mib::qk_norm_rope(qkv, tokens, ld_token, seq_len, q_heads, kv_heads, head_dim, q_norm, k_norm, eps,
+                                    cos_table, sin_table, q_out, k_out, v_out, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "qk_norm_rope launch");
   return MIB_OK;
 }
 

@@ -25,6 +25,7 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
+from . import _native as N
 from .crossbar_shard import ColumnShardedLinearMem, RowShardedLinearMem, shard_bounds
 
 
@@ -123,14 +124,14 @@ class Qwen3CimLayer(torch.nn.Module):
         xs = self.qkv_proj.new_input()
         self.engine.slice_rmsnorm_input(xs, h, self.in_norm, a.eps)
         qkv = self.qkv_proj.forward_sliced(xs)
-        nq, nk = self.local_heads * a.head_dim, self.local_kv * a.head_dim
-        q = qkv[..., :nq].reshape(B, T, self.local_heads, a.head_dim)
-        k = qkv[..., nq:nq + nk].reshape(B, T, self.local_kv, a.head_dim)
-        v = qkv[..., nq + nk:].reshape(B, T, self.local_kv, a.head_dim)
-        q = apply_rope(rms_norm(q, self.q_norm, a.eps), cos, sin).transpose(1, 2)
-        k = apply_rope(rms_norm(k, self.k_norm, a.eps), cos, sin).transpose(1, 2)
-        v = v.transpose(1, 2)
-        o = F.scaled_dot_product_attention(q.bfloat16(), k.bfloat16(), v.bfloat16(), is_causal=True,
+        # q/k RMSNorm, rotary embedding and bf16 casts in one pass (mib_qk_norm_rope_bf16); the torch
+        # form is rope(rms_norm(q, q_norm)) etc. (rms_norm, apply_rope above)
+        q, k, v = (torch.empty(B, T, n, a.head_dim, dtype=torch.bfloat16, device=h.device)
+                   for n in (self.local_heads, self.local_kv, self.local_kv))
+        N.call("mib_qk_norm_rope_bf16", N.ptr(qkv), B * T, qkv.stride(-2), T, self.local_heads, self.local_kv,
+               a.head_dim, N.ptr(self.q_norm), N.ptr(self.k_norm), float(a.eps), N.ptr(cos), N.ptr(sin), N.ptr(q),
+               N.ptr(k), N.ptr(v), N.stream_ptr(h.device))
+        o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
                                            enable_gqa=self.local_heads != self.local_kv)
         o = o.transpose(1, 2).reshape(B, T, self.local_heads * a.head_dim).float()
         h = h + self.o_proj(o)
@@ -177,8 +178,7 @@ class Qwen3CimPrefill(torch.nn.Module):
         B, T = ids.shape
         if T not in self._rope:
             self._rope[T] = rope_cache(T, a.head_dim, a.rope_theta, ids.device)
-        cos, sin = self._rope[T]
-        cos, sin = cos[:, None, :], sin[:, None, :]          # (T, 1, head_dim): broadcast over heads
+        cos, sin = self._rope[T]                             # (T, head_dim) each
         h = F.embedding(ids, self.embed)
         for layer in self.layers:
             h = layer(h, cos, sin)

@@ -93,3 +93,32 @@ def test_fused_input_feeds_mvm(cuda):
         torch.cuda.synchronize()
         rel = float((yf - yr).norm() / yr.norm())
         assert rel <= 2e-3, rel        # a few codes differ by one step (reordered sum of squares)
+
+
+@pytest.mark.parametrize("hq,hk,d", [(16, 8, 128), (4, 4, 64)])
+def test_qk_norm_rope_bf16(hq, hk, d, cuda):
+    """mib_qk_norm_rope_bf16 equals rope(rms_norm(q) * q_norm), rope(rms_norm(k) * k_norm) and v cast to
+    bf16, computed in fp32 by torch (one bf16 rounding step at most, from the reordered sum of squares)."""
+    from memintelli_flash_b200 import _native as N
+    from memintelli_flash_b200.qwen3_prefill import apply_rope, rms_norm, rope_cache
+    B, T = 2, 96
+    g = torch.Generator(device=cuda).manual_seed(13)
+    qkv = torch.randn(B, T, (hq + 2 * hk) * d, device=cuda, generator=g)
+    qn = torch.rand(d, device=cuda, generator=g) + 0.5
+    kn = torch.rand(d, device=cuda, generator=g) + 0.5
+    cos, sin = rope_cache(T, d, 1e6, cuda)
+    q, k, v = (torch.empty(B, T, n, d, dtype=torch.bfloat16, device=cuda) for n in (hq, hk, hk))
+    N.call("mib_qk_norm_rope_bf16", N.ptr(qkv), B * T, qkv.stride(-2), T, hq, hk, d, N.ptr(qn), N.ptr(kn), 1e-6,
+           N.ptr(cos), N.ptr(sin), N.ptr(q), N.ptr(k), N.ptr(v), N.stream_ptr(cuda))
+    rq = apply_rope(rms_norm(qkv[..., :hq * d].reshape(B, T, hq, d), qn, 1e-6), cos[:, None], sin[:, None])
+    rk = apply_rope(rms_norm(qkv[..., hq * d:(hq + hk) * d].reshape(B, T, hk, d), kn, 1e-6), cos[:, None],
+                    sin[:, None])
+    rv = qkv[..., (hq + hk) * d:].reshape(B, T, hk, d)
+    assert torch.equal(v, rv.bfloat16())
+    for got, want in ((q, rq), (k, rk)):
+        w16 = want.bfloat16()
+        # one bf16 step, or 1e-4 absolute where rope's x*cos + rot*sin cancels to a value near zero (the
+        # normalised values are O(1), so fp32 differences of ~1e-7 there exceed a step of the result)
+        step = (w16.float().abs() * 2.0 ** -7).clamp_min(1e-4)
+        assert ((got.float() - w16.float()).abs() <= step).all()
+        assert (got != w16).float().mean().item() <= 1e-2
