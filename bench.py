@@ -194,6 +194,20 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def dp_tp_layout(world, rank, batch, tp=0):
+    """(tp, dp, tp groups as rank lists, this rank's [first, end) sequence range).  Ranks form dp groups
+    of tp consecutive ranks; tp == 0 picks pure data parallelism when the batch divides by the rank
+    count, else one group of all ranks."""
+    if tp <= 0:
+        tp = 1 if batch % world == 0 else world
+    if world % tp or batch % (world // tp):
+        raise SystemExit(f"--tp {tp} does not divide {world} ranks into groups that split {batch} sequences")
+    dp = world // tp
+    per = batch // dp
+    g = rank // tp
+    return tp, dp, [list(range(r * tp, (r + 1) * tp)) for r in range(dp)], (g * per, (g + 1) * per)
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -206,19 +220,42 @@ def run_b200(args):
     if world > 1:
         import datetime
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+        # high-priority NCCL streams: the overlapped all-reduces get SMs ahead of the queued MVM tiles
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.is_high_priority_stream = True
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300), pg_options=opts)
 
     from memintelli_flash_b200 import DPETensor
     from memintelli_flash_b200 import _native as N
     from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
 
+    # dp x tp: ranks form dp groups of tp consecutive ranks; a group shards every crossbar across its tp
+    # ranks (crossbar_shard) and takes BATCH/dp of the sequences.  --tp 0 picks pure dp when the batch
+    # divides by the rank count (no collective on the data path), else pure tp.
+    tp, dp, groups, (s0, s1) = dp_tp_layout(world, rank, BATCH, args.tp)
+    tp_group = None
+    if world > 1:
+        for r, ranks in enumerate(groups):        # every rank creates every group, in the same order
+            grp = dist.new_group(ranks)
+            if rank // tp == r:
+                tp_group = grp
     torch.manual_seed(1234 + rank)
     engine = DPETensor(device=dev, **ENGINE)
-    model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev)
+    model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=tp_group)
     torch.cuda.synchronize()
     g = torch.Generator().manual_seed(1)
     ids_host = torch.randint(0, ARCH["vocab"], (BATCH, SEQ), generator=g).pin_memory()
+    ids_host = ids_host[s0:s1]                    # this dp group's sequences
     ids = ids_host.to(dev)
+
+    def step(x):
+        """One prefill step: the group's mean loss, averaged over the dp groups."""
+        loss = model(x)
+        if world > 1:
+            loss = loss.reshape(1)
+            dist.all_reduce(loss)              # tp ranks hold the same loss: the sum / world is the dp mean
+            loss = loss[0] / world
+        return loss
 
     def barrier():
         if world > 1:
@@ -226,7 +263,7 @@ def run_b200(args):
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        model(ids)
+        step(ids)
     barrier()
     # ---- device-resident timed region
     engine.launch_log = []
@@ -236,7 +273,7 @@ def run_b200(args):
         barrier()
         t_start.record()
         for _ in range(args.steps):
-            loss = model(ids)
+            loss = step(ids)
         t_end.record()
         barrier()
     launches = N.launch_count() - launches0
@@ -257,7 +294,7 @@ def run_b200(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        loss_host = model(ids_host.to(dev, non_blocking=True)).item()
+        loss_host = step(ids_host.to(dev, non_blocking=True)).item()
     e1.record()
     barrier()
     e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
@@ -277,7 +314,7 @@ def run_b200(args):
                 "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
                 "config": {"workload": "Qwen3-0.6B-arch CIM prefill, 8x2048 tokens, 197 CIM linears",
                            "model": "Qwen3-0.6B-arch (random init)", "global_batch": BATCH, "seq_len": SEQ,
-                           "parallelism": f"crossbar-shard{world}" if world > 1 else "single",
+                           "parallelism": f"dp{dp}xtp{tp}" if world > 1 else "single",
                            "l2": "inputs larger than L2 (3 GB of programmed crossbars per forward)",
                            "engine": ENGINE},
                 "sliced_mvm_tops": ops_per_token() * BATCH * SEQ * args.steps / (ms / 1000.0) / 1e12,
@@ -310,6 +347,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="ranks per crossbar-sharding group (0: pure data parallel when the batch divides by the "
+                         "rank count, else all ranks shard)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -87,6 +87,11 @@ class _ShardBase(torch.nn.Module):
         """``forward`` for an input already sliced by a fused producer."""
         return self._finish(self.local.forward_sliced(input_sliced))
 
+    def partial_sliced(self, input_sliced):
+        """This rank's output before any collective (row sharding: the partial sum; the caller
+        all-reduces it and adds ``full_bias``)."""
+        return self.local.forward_sliced(input_sliced)
+
 
 class _LinearFromWeight(LinearMem):
     """LinearMem programmed from a given weight (no random init, programmed once)."""

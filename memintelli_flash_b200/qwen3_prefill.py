@@ -119,6 +119,16 @@ class Qwen3CimLayer(torch.nn.Module):
         """One decoder layer.  The RMSNorms before the q/k/v and gate/up crossbars and the SwiGLU
         before the down crossbar run inside the input slicing (``DPETensor.slice_rmsnorm_input`` /
         ``slice_swiglu_input``), so those activations are never written out."""
+        h = h + self._reduce(self.attn_partial(h, cos, sin))
+        return h + self._reduce(self.mlp_partial(h))
+
+    def _reduce(self, y):
+        if self.o_proj.world > 1:
+            dist.all_reduce(y, group=self.o_proj.group)
+        return y
+
+    def attn_partial(self, h, cos, sin):
+        """Attention block up to this rank's o_proj partial sum (before the all-reduce)."""
         a = self.arch
         B, T, _ = h.shape
         xs = self.qkv_proj.new_input()
@@ -134,13 +144,18 @@ class Qwen3CimLayer(torch.nn.Module):
         o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
                                            enable_gqa=self.local_heads != self.local_kv)
         o = o.transpose(1, 2).reshape(B, T, self.local_heads * a.head_dim).float()
-        h = h + self.o_proj(o)
+        xs = self.o_proj.new_input()
+        xs.slice_data_imp(self.engine, o)
+        return self.o_proj.partial_sliced(xs)
+
+    def mlp_partial(self, h):
+        """SwiGLU MLP up to this rank's down_proj partial sum (before the all-reduce)."""
         xs = self.gate_up_proj.new_input()
-        self.engine.slice_rmsnorm_input(xs, h, self.post_norm, a.eps)
+        self.engine.slice_rmsnorm_input(xs, h, self.post_norm, self.arch.eps)
         gu = self.gate_up_proj.forward_sliced(xs)
         ms = self.down_proj.new_input()
         self.engine.slice_swiglu_input(ms, gu, self.local_inter)
-        return h + self.down_proj.forward_sliced(ms)
+        return self.down_proj.partial_sliced(ms)
 
 
 class Qwen3CimPrefill(torch.nn.Module):
@@ -151,6 +166,9 @@ class Qwen3CimPrefill(torch.nn.Module):
         super().__init__()
         device = device or engine.device
         self.arch, self.group, self.engine = arch, group, engine
+        # sequences per forward are processed in this many groups when sharded, so that each group's
+        # all-reduces overlap the other groups' crossbar work (see _layers_overlapped)
+        self.micro_batches = 2
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         gen = torch.Generator(device=device)
@@ -180,13 +198,45 @@ class Qwen3CimPrefill(torch.nn.Module):
             self._rope[T] = rope_cache(T, a.head_dim, a.rope_theta, ids.device)
         cos, sin = self._rope[T]                             # (T, head_dim) each
         h = F.embedding(ids, self.embed)
-        for layer in self.layers:
-            h = layer(h, cos, sin)
+        if self.world > 1 and self.micro_batches > 1 and B >= self.micro_batches:
+            h = self._layers_overlapped(h, cos, sin)
+        else:
+            for layer in self.layers:
+                h = layer(h, cos, sin)
         xs = self.lm_head.new_input()
         self.engine.slice_rmsnorm_input(xs, h[:, :-1], self.norm, a.eps)
         logits = self.lm_head.forward_sliced(xs)             # (B, T-1, V_local)
         target = ids[:, 1:]
         return self._sharded_ce(logits, target)
+
+    def _layers_overlapped(self, h, cos, sin):
+        """The decoder layers over ``micro_batches`` groups of sequences, with every o/down all-reduce
+        asynchronous: a group's all-reduce runs while the other groups' crossbars compute, and is
+        waited for only where that group next needs its hidden state.  Per token the arithmetic is
+        that of ``Qwen3CimLayer.forward``."""
+        hs = list(torch.chunk(h, self.micro_batches, dim=0))
+        pending = [None] * len(hs)          # (partial output, all-reduce work) per group
+
+        def settle(m):
+            if pending[m] is not None:
+                y, work = pending[m]
+                work.wait()
+                hs[m] = hs[m] + y
+                pending[m] = None
+
+        def launch(m, y):
+            pending[m] = (y, dist.all_reduce(y, group=self.group, async_op=True))
+
+        for layer in self.layers:
+            for m in range(len(hs)):
+                settle(m)
+                launch(m, layer.attn_partial(hs[m], cos, sin))
+            for m in range(len(hs)):
+                settle(m)
+                launch(m, layer.mlp_partial(hs[m]))
+        for m in range(len(hs)):
+            settle(m)
+        return torch.cat(hs, dim=0)
 
     def _sharded_ce(self, logits, target):
         """Mean cross-entropy over column-sharded logits (no gather of the vocabulary)."""
