@@ -118,3 +118,20 @@ def test_mvm_rejects_bad_arguments_before_any_device_work():
     rc = N.lib().mib_mvm(None, None, 10, xs, None, None, 10, ws, _kg(128), _dev(4096), 0, None, 0, None, None,
                          None, None, None, 0, None)
     assert rc == N.MIB_ERR_PARAM
+
+
+def test_fused_producers_and_attention_prep_check_arguments_on_the_host():
+    L = N.lib()
+    fake = ctypes.c_void_p(0x1000)          # never dereferenced: every call below fails its host checks
+    xs = _spec(SM, (1, 32), (1, 128))
+    assert L.mib_slice_rmsnorm_input(None, 1, 4, 128, 512, 128, fake, 1e-6, xs, _kg(128), 4, 0, fake, fake, fake,
+                                     None, None, None) == N.MIB_ERR_PARAM
+    assert L.mib_slice_rmsnorm_input(fake, 1, 4, 128, 512, 128, None, 1e-6, xs, _kg(128), 4, 0, fake, fake, fake,
+                                     None, None, None) == N.MIB_ERR_PARAM
+    assert L.mib_slice_swiglu_input(fake, 1, 4, 128, 1024, 256, 64, xs, _kg(128), 4, 0, fake, fake, fake, None,
+                                    None, None) == N.MIB_ERR_SHAPE
+    assert b"overlap" in L.mib_last_error()
+    args = (fake, 8, 4096, 8, 16, 8, 128, fake, fake, 1e-6, fake, fake, fake, fake, fake, None)
+    assert L.mib_qk_norm_rope_bf16(*args[:6], 96, *args[7:]) == N.MIB_ERR_UNSUPPORTED
+    assert L.mib_qk_norm_rope_bf16(fake, 8, 4000, *args[3:]) == N.MIB_ERR_SHAPE
+    assert L.mib_qk_norm_rope_bf16(None, *args[1:]) == N.MIB_ERR_PARAM
