@@ -130,6 +130,15 @@ class SlicedData(object):
 
     # ------------------------------------------------------------------ helpers
     def _spec(self) -> N.SliceSpec:
+        """ctypes slice spec; cached in the buffer dict, so slicing again rebuilds it."""
+        cached = self._buf.get("spec_c")
+        if cached is not None and cached[0] is self.slice_method:
+            return cached[1]
+        sp = self._make_spec()
+        self._buf["spec_c"] = (self.slice_method, sp)
+        return sp
+
+    def _make_spec(self) -> N.SliceSpec:
         g = self._buf["geom"]
         sm = self._slices()
         sp = N.SliceSpec()
@@ -142,9 +151,12 @@ class SlicedData(object):
         return sp
 
     def _kgeom(self) -> N.KGeom:
-        g = self._buf["geom"]
-        kg = N.KGeom()
-        kg.k, kg.kp, kg.p, kg.pp, kg.kt = g["k"], g["kp"], g["p"], g["pp"], g["kt"]
+        kg = self._buf.get("kgeom_c")
+        if kg is None:
+            g = self._buf["geom"]
+            kg = N.KGeom()
+            kg.k, kg.kp, kg.p, kg.pp, kg.kt = g["k"], g["kp"], g["p"], g["pp"], g["kt"]
+            self._buf["kgeom_c"] = kg
         return kg
 
     @property

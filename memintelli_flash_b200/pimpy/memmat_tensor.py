@@ -101,6 +101,18 @@ class DPETensor(object):
         return self.vnoise > 0 or self.write_variation > 0 or any(s > 0 for s in self._sigmas())
 
     def _device_spec(self) -> N.DeviceSpec:
+        """ctypes device spec, rebuilt only when an attribute it reads has changed."""
+        radc = tuple(int(v) for v in self.radc.tolist()) if self.radc_is_list else int(self.radc)
+        key = (self.HGS, self.LGS, self.g_level, self.rdac, radc, self.vread, self.vnoise, self.write_variation,
+               self.rate_stuck_HGS, self.rate_stuck_LGS, tuple(self._sigmas()))
+        cached = getattr(self, "_dspec_cache", None)
+        if cached is not None and cached[0] == key:
+            return cached[1]
+        d = self._make_device_spec()
+        self._dspec_cache = (key, d)
+        return d
+
+    def _make_device_spec(self) -> N.DeviceSpec:
         d = N.DeviceSpec()
         d.hgs, d.lgs = float(self.HGS), float(self.LGS)
         d.g_level, d.rdac = int(self.g_level), int(self.rdac)
