@@ -184,14 +184,20 @@ def run_reference(args):
             "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "n_cores": cores,
             "impl": "reference",
-            "config": {"workload": "Qwen3-0.6B-arch CIM prefill 8x2048 (bounded CPU sample per step)",
-                       "global_batch": BATCH, "seq_len": SEQ, "parallelism": "cpu"},
+            "config": dict(base_config(), parallelism="cpu (host cores)",
+                           sample="bounded per step, extrapolated by slice-pair op count"),
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
                              "sample": "per step: one decoder layer's 7 CIM linears + 1024x4096 lm_head slice on "
                                        "256 tokens (torch-CPU restatement of _dot_inference with read noise), "
                                        "extrapolated by slice-pair op count"},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def base_config():
+    """The workload keys both arms report."""
+    return {"workload": "Qwen3-0.6B-arch CIM prefill, 8x2048 tokens, 197 CIM linears",
+            "model": "Qwen3-0.6B-arch (random init)", "global_batch": BATCH, "seq_len": SEQ, "engine": ENGINE}
 
 
 def dp_tp_layout(world, rank, batch, tp=0):
@@ -312,11 +318,8 @@ def run_b200(args):
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-                "config": {"workload": "Qwen3-0.6B-arch CIM prefill, 8x2048 tokens, 197 CIM linears",
-                           "model": "Qwen3-0.6B-arch (random init)", "global_batch": BATCH, "seq_len": SEQ,
-                           "parallelism": f"dp{dp}xtp{tp}" if world > 1 else "single",
-                           "l2": "inputs larger than L2 (3 GB of programmed crossbars per forward)",
-                           "engine": ENGINE},
+                "config": dict(base_config(), parallelism=f"dp{dp}xtp{tp}" if world > 1 else "single",
+                               l2="inputs larger than L2 (3 GB of programmed crossbars per forward)"),
                 "sliced_mvm_tops": ops_per_token() * BATCH * SEQ * args.steps / (ms / 1000.0) / 1e12,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak, "traffic": None, "peak_kind": f"bf16 sustained ({peak_kind})",
