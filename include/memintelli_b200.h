@@ -185,10 +185,13 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
             float* workspace, int64_t workspace_floats, cudaStream_t stream);
 
 /* Split-K workspace for mib_mvm, in floats (0 when the output tiles already fill the GPU).
- * When fewer than ~3/4 of the 148 SMs would get an output tile, mib_mvm divides the K tiles
- * into contiguous ranges, writes one fp32 partial output per range into `workspace`
- * ([splits][M][N]) and adds them in a fixed order (deterministic).  A NULL or smaller
- * workspace runs the MVM without splitting. */
+ * mib_mvm divides the K tiles into contiguous ranges in two cases:
+ *   - fewer than ~3/4 of the 148 SMs would get an output tile;
+ *   - the grid spans up to 4 waves and the last wave is partly idle.  It then uses the 2-4
+ *     ranges that cut the wave-rounded time by at least 10% (e.g. 2048 x 1024 outputs).
+ * It writes one fp32 partial output per range into `workspace` ([splits][M][N]) and adds them
+ * in a fixed order (deterministic).  A NULL or smaller workspace runs the MVM without
+ * splitting. */
 int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
                       const mib_k_geom* kg, const mib_device_spec* dev, int64_t* floats_out);
 
@@ -198,8 +201,9 @@ int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const 
  * result as mib_mvm without the workspace (and without the acc_dump test hook).  When
  * the output tiles fill less of the GPU than split-K needs, the split-K partials go to
  * a scratch array built into this library: 2^20 floats (4 MiB), held on every GPU that
- * loads the library until the process exits.  Problems whose split-K scratch
- * (mib_mvm_workspace) exceeds 2^20 floats are rejected with MIB_ERR_UNSUPPORTED.
+ * loads the library until the process exits.  Problems whose underfilled-grid split needs
+ * more than 2^20 floats are rejected with MIB_ERR_UNSUPPORTED.  The wave-balancing split
+ * of mib_mvm is not used here; those problems run unsplit.
  * The first call on a device resolves the array's device address (cudaGetSymbolAddress),
  * so make that first call before any stream capture.  The array is shared by every call
  * and keeps the last call's contents (every split overwrites all of its partials before

@@ -268,21 +268,45 @@ struct SplitPlan {
   int tiles_per_split = 0;
 };
 
-SplitPlan split_plan(int64_t m, int64_t n, int64_t kt, int flush, int sy) {
+// Contiguous K ranges of whole flush groups; `want` ranges at most.
+static SplitPlan split_ranges(int64_t kt, int flush, int64_t groups, int64_t want) {
   SplitPlan sp;
   sp.tiles_per_split = static_cast<int>(kt);
-  const int64_t bn = 16 * mib::mvm_column_groups(sy);
-  const int64_t ctas = ((n + bn - 1) / bn) * ((m + mib::kMvmBM - 1) / mib::kMvmBM);
-  const int64_t groups = (kt + flush - 1) / flush;
-  if (ctas * 4 >= 148 * 3 || groups < 2) return sp;
-  int64_t want = (148 + ctas - 1) / ctas;
   if (want > groups) want = groups;
   if (want > 32) want = 32;
+  if (want < 2) return sp;
   const int64_t per = (groups + want - 1) / want;           // flush groups per split
   sp.tiles_per_split = static_cast<int>(per * flush);
   sp.splits = static_cast<int>((kt + sp.tiles_per_split - 1) / sp.tiles_per_split);
   if (sp.splits < 2) sp = SplitPlan{1, static_cast<int>(kt)};
   return sp;
+}
+
+// Two cases split K:
+//  * a grid under 3/4 of the 148 SMs: enough splits to fill them;
+//  * with `balance`, a grid of up to 4 waves whose last wave is partly idle: the split
+//    count (2..4) that minimises the wave-rounded time, if it saves at least 10%.  For
+//    example, 352 output tiles take 3 waves unsplit and 5 half-length waves split in two.
+SplitPlan split_plan(int64_t m, int64_t n, int64_t kt, int flush, int sy, bool balance) {
+  const int64_t bn = 16 * mib::mvm_column_groups(sy);
+  const int64_t ctas = ((n + bn - 1) / bn) * ((m + mib::kMvmBM - 1) / mib::kMvmBM);
+  const int64_t groups = (kt + flush - 1) / flush;
+  if (groups < 2) return split_ranges(kt, flush, groups, 1);
+  if (ctas * 4 < 148 * 3) return split_ranges(kt, flush, groups, (148 + ctas - 1) / ctas);
+  if (!balance || ctas >= 4 * 148) return split_ranges(kt, flush, groups, 1);
+  SplitPlan best = split_ranges(kt, flush, groups, 1);
+  double best_cost = static_cast<double>((ctas + 147) / 148);
+  const double unsplit = best_cost;
+  for (int64_t want = 2; want <= 4; ++want) {
+    const SplitPlan sp = split_ranges(kt, flush, groups, want);
+    if (sp.splits < 2) continue;
+    const double cost = static_cast<double>((ctas * sp.splits + 147) / 148) / sp.splits;
+    if (cost < best_cost) {
+      best = sp;
+      best_cost = cost;
+    }
+  }
+  return best_cost <= 0.9 * unsplit ? best : split_ranges(kt, flush, groups, 1);
 }
 
 }  // namespace
@@ -539,17 +563,23 @@ int mib_adc_plan(const mib_slice_spec* x_spec, const mib_slice_spec* w_spec, con
   return MIB_OK;
 }
 
-int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
-                      const mib_k_geom* kg, const mib_device_spec* dev, int64_t* floats_out) {
+// Split-K scratch in floats for the plan with (mib_mvm) or without (built-in scratch) wave balancing.
+static int split_workspace_floats(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
+                            const mib_k_geom* kg, const mib_device_spec* dev, bool balance, int64_t* floats_out) {
   SliceTab tx, tw;
   if (int r = make_tab(x_spec, tx)) return r;
   if (int r = make_tab(w_spec, tw)) return r;
   if (!kg || !dev || !floats_out) return fail(MIB_ERR_PARAM, "NULL argument");
   AdcPlan pl;
   if (int r = adc_plan(tx, tw, x_spec, w_spec, kg, dev, pl)) return r;
-  const SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S);
+  const SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S, balance);
   *floats_out = sp.splits > 1 ? static_cast<int64_t>(sp.splits) * m * n : 0;
   return MIB_OK;
+}
+
+int mib_mvm_workspace(int64_t m, int64_t n, const mib_slice_spec* x_spec, const mib_slice_spec* w_spec,
+                      const mib_k_geom* kg, const mib_device_spec* dev, int64_t* floats_out) {
+  return split_workspace_floats(m, n, x_spec, w_spec, kg, dev, true, floats_out);
 }
 
 int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_slice_spec* x_spec,
@@ -627,7 +657,7 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   a.col_stride = layout->col_stride;
   a.bias = bias;
   a.acc_dump = acc_dump;
-  SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S);
+  SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S, true);
   if (sp.splits > 1 && (!workspace || workspace_floats < static_cast<int64_t>(sp.splits) * m * n))
     sp = SplitPlan{1, static_cast<int>(kg->kt)};
   a.tiles_per_split = sp.tiles_per_split;
@@ -690,8 +720,10 @@ extern "C" int mib_mvm_static_scratch(const void* a_planes, const float* a_scale
                                       const mib_device_spec* dev, int32_t operand_kind, const int32_t* adc_table,
                                       int32_t adc_table_len, float* y, const mib_out_layout* layout,
                                       const float* bias, cudaStream_t stream) {
+  // Scratch is needed only where the grid underfills the GPU; the optional wave-balancing split
+  // of mib_mvm is skipped here (mib_mvm runs unsplit when handed no or too little workspace).
   int64_t need = 0;
-  if (int r = mib_mvm_workspace(m, n, x_spec, w_spec, kg, dev, &need)) return r;
+  if (int r = split_workspace_floats(m, n, x_spec, w_spec, kg, dev, false, &need)) return r;
   if (need > kStaticScratchFloats) {
     char buf[200];
     snprintf(buf, sizeof(buf),

@@ -92,6 +92,17 @@ def test_split_k_workspace_choice():
     assert f.value == 0                                           # 8192 output tiles: no split
 
 
+def test_split_k_balances_a_partly_idle_last_wave():
+    """352 output tiles (2048 x 1024 at 48 columns) fill 2.38 waves of 148 SMs: split in two they run as
+    5 half-length waves instead of 3 full ones, so the plan asks for two partial outputs."""
+    xs, ws, dev = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 32), (128, 128)), _dev(4096)
+    f = N.c_i64(-1)
+    assert N.lib().mib_mvm_workspace(2048, 1024, xs, ws, _kg(2048), dev, f) == 0
+    assert f.value == 2 * 2048 * 1024
+    assert N.lib().mib_mvm_workspace(4096, 1024, xs, ws, _kg(2048), dev, f) == 0
+    assert f.value == 0                                           # 704 tiles: 4.76 waves, a split saves < 10%
+
+
 def test_adc_plan_noisy_skips_table():
     rc, mode, n = _plan(_spec(SM, (1, 32), (1, 64)), _spec(SM, (32, 32), (64, 64)), _kg(100, qg=64),
                         _dev(1024, sigma=0.05))
