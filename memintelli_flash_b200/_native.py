@@ -128,7 +128,20 @@ def ptr(t):
 
 
 def stream_ptr(device=None):
+    """The current CUDA stream of ``device`` (a torch.device, an index or None for the current
+    device) as a cudaStream_t.  Uses torch's raw-stream query when it is there: the public
+    ``torch.cuda.current_stream`` costs several microseconds per call on the per-layer host path."""
     import torch
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        if device is None:
+            idx = torch.cuda.current_device()
+        elif isinstance(device, int):
+            idx = device
+        else:
+            device = torch.device(device)
+            idx = device.index if device.index is not None else torch.cuda.current_device()
+        return ctypes.c_void_p(raw(idx))
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
