@@ -1,6 +1,6 @@
 """Benchmark: CIM Qwen3-0.6B-architecture prefill on B200 (tokens/s), one process per GPU.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference]
+    python bench.py [--gpus N --steps K --warmup W] [--impl b200|reference] [--tp T]
     torchrun --nproc-per-node N bench.py --gpus N ...
 
 Workload: 8 sequences x 2048 token ids, uniform over the 151936-token
@@ -10,12 +10,20 @@ architecture (28 layers, hidden 1024, 16/8 heads x 128, SwiGLU 3072) whose
 engine: slices [1,1,2,2,2], weight quant_gran (128,128) / paral (32,32),
 input quant_gran (1,128) / paral (1,32), radc 4096, and the device model of
 the reference's Qwen3 example (HGS 1e-5, LGS 1e-8, 4 levels, rdac 4, read
-variation 0.05).  A step is one full prefill forward with loss.  With N GPUs
-every crossbar is sharded across the ranks (strong scaling of one forward).
+variation 0.05).  A step is one full prefill forward with loss.
 
-``--impl reference`` times the CPU restatement of the reference algorithm on
-the host cores on a bounded sample of the same workload and extrapolates to
-the metric's unit.
+With N GPUs the headline layout is data parallel over the 8 sequences (every
+rank holds all crossbars, no collective on the data path but the loss mean);
+``--tp T`` shards every crossbar over groups of T ranks instead.  At N > 1 the
+line also carries ``tp``: the same workload with every crossbar sharded over
+all N ranks (column-sharded q/k/v, gate/up and lm_head, row-sharded o and
+down), and ``layout_check``: the noise-free loss of both layouts, which must
+agree to fp32 summation order.
+
+``--impl reference`` times the reference's algorithm (the oracle's torch
+restatement of ``_dot_inference``) on the host cores on a bounded sample of
+the same workload and extrapolates to the metric's unit; with a GPU present it
+also times the same restatement on cuda:0 (``reference_gpu``).
 """
 from __future__ import annotations
 
@@ -163,14 +171,48 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------------------------
+def gpu_reference_sample(tokens: int = 2048, head_cols: int = 4096, seed: int = 0, reps: int = 2):
+    """The reference's algorithm on cuda:0: the torch restatement of ``_dot_inference`` (per slice pair a
+    batched contraction into a (Kt, M, Np) partial, ADC, shift-add, block rescale, K-tile sum, read noise
+    per call) over one decoder layer's 7 linears plus a lm_head column slice on ``tokens`` tokens.
+    Operands are prepared (sliced) beforehand and only the device work is timed, which flatters the
+    reference.  Returns (seconds per pass, slice-pair ops per pass)."""
+    import torch
+    from oracle import cim_oracle as O
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(seed)
+    eng = O.Engine(**ENGINE)
+    sm = [1, 1, 2, 2, 2]
+    prepared, ops = [], 0.0
+    for k, n in LAYER_LINEARS + [(LM_HEAD[0], head_cols)]:
+        w = (rng.standard_normal((k, n)) * 0.02).astype(np.float32)
+        x = rng.standard_normal((tokens, k)).astype(np.float32)
+        xs = O.slice_matrix(x, sm, None, (1, 32), (1, 128))
+        ws = O.slice_matrix(w, sm, None, (32, 32), (128, 128))
+        prepared.append(O.torch_port_operands(xs, ws, eng, dev))
+        ops += 2.0 * tokens * xs.geom.cols_p * ws.geom.cols_p * 25
+    for o in prepared:                                   # warm-up
+        O.torch_port_mvm(o, eng, seed)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for r in range(reps):
+        for o in prepared:
+            O.torch_port_mvm(o, eng, seed + r)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / 1000.0 / reps, ops
+
+
 def run_reference(args):
-    """--impl reference: the CPU restatement, rank 0 only."""
+    """--impl reference: the reference's algorithm on the host cores (and on cuda:0 when present),
+    rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     cores = os.cpu_count() or 1
     import torch
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(cores)
     for _ in range(args.warmup):
         cpu_sample(seed=99, tokens=32)
     times = []
@@ -180,17 +222,23 @@ def run_reference(args):
         times.append(sec)
     rate = ops * len(times) / sum(times)
     value = rate / ops_per_token()
+    sample = ("per step: one decoder layer's 7 CIM linears + 1024x4096 lm_head slice on 256 tokens (torch "
+              "restatement of _dot_inference with read noise, slicing included), extrapolated by slice-pair op "
+              "count")
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "n_cores": cores,
-            "impl": "reference",
-            "config": dict(base_config(), parallelism="cpu (host cores)",
-                           sample="bounded per step, extrapolated by slice-pair op count"),
-            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                             "sample": "per step: one decoder layer's 7 CIM linears + 1024x4096 lm_head slice on "
-                                       "256 tokens (torch-CPU restatement of _dot_inference with read noise), "
-                                       "extrapolated by slice-pair op count"},
+            "impl": "reference", "config": dict(base_config(), parallelism="cpu (host cores)", sample=sample),
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if torch.cuda.is_available():
+        sec, gops = gpu_reference_sample()
+        line["reference_gpu"] = {
+            "value": gops / sec / ops_per_token(), "unit": "tokens/s", "device": torch.cuda.get_device_name(0),
+            "kind": "port", "sliced_mvm_tops": gops / sec / 1e12,
+            "sample": "one decoder layer's 7 CIM linears + 1024x4096 lm_head slice on 2048 tokens, the torch "
+                      "restatement of _dot_inference on cuda:0 (MVM device work only, operands pre-sliced), "
+                      "extrapolated by slice-pair op count"}
     print(json.dumps(line), flush=True)
 
 
@@ -214,6 +262,89 @@ def dp_tp_layout(world, rank, batch, tp=0):
     return tp, dp, [list(range(r * tp, (r + 1) * tp)) for r in range(dp)], (g * per, (g + 1) * per)
 
 
+# Epilogue ceiling of the fused MVM: every ADC event costs one integer multiply-add (FMA-heavy pipe) and
+# half of a packed f32x2 rounding FMA, of which the FMA-heavy pipe takes half: 1.5 FMA-heavy lane operations
+# per event at 64 lanes per clock per SM (16 per sub-partition) caps it at 42.7 events per SM clock.
+MVM_FMAHEAVY_OPS_PER_ADC_EVENT = 1.5
+# DRAM bytes per ADC event of the fused MVM (dram__bytes_read.sum + dram__bytes_write.sum of one launch
+# divided by its ADC events), from the capture in profiles/mvm_kernel_4096.md; the bench scales it by the
+# ADC events of its launches.
+MVM_DRAM_BYTES_PER_ADC_EVENT = (1.48e9 + 68e6) / 5.369e10
+
+
+class Layout:
+    """One layout of the workload on this rank: a model, its process group and its share of the ids."""
+
+    def __init__(self, model, ids_host, dev, world, group_world):
+        self.model, self.world, self.group_world = model, world, group_world
+        self.ids_host = ids_host
+        self.ids = ids_host.to(dev)
+
+    def step(self, x):
+        """One prefill step: the group's mean loss, averaged over all ranks' groups."""
+        import torch.distributed as dist
+        loss = self.model(x)
+        if self.world > 1:
+            loss = loss.reshape(1)
+            dist.all_reduce(loss)       # ranks of one group hold the same loss: the sum / world is the mean
+            loss = loss[0] / self.world
+        return loss
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def time_layout(lay: Layout, engine, args, world, local, dev, clocks=False):
+    """Warm-up, then the device-resident timed region (CUDA events, max over ranks) and the end-to-end
+    region (host ids in, host loss out, every step).  Returns a dict of measurements."""
+    import torch
+    import torch.distributed as dist
+    from memintelli_flash_b200 import _native as N
+    for _ in range(args.warmup):
+        lay.step(lay.ids)
+    barrier(world)
+    engine.launch_log = []
+    launches0 = N.launch_count()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local) if clocks else None
+    if clk:
+        clk.__enter__()
+    barrier(world)
+    t_start.record()
+    for _ in range(args.steps):
+        loss = lay.step(lay.ids)
+    t_end.record()
+    barrier(world)
+    if clk:
+        clk.__exit__()
+    launches = N.launch_count() - launches0
+    ms = t_start.elapsed_time(t_end)
+    log, engine.launch_log = engine.launch_log, None
+    mvm_ms = sum(a.elapsed_time(b) for a, b, _, _ in log)
+    t = torch.tensor([ms, mvm_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t[0])
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss_host = lay.step(lay.ids_host.to(dev, non_blocking=True)).item()
+    e1.record()
+    barrier(world)
+    e2e = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e, op=dist.ReduceOp.MAX)
+    return dict(ms=ms_max, mvm_ms=mvm_ms, mvm_ops=sum(o for _, _, o, _ in log), mvm_adc=sum(e for _, _, _, e in log),
+                launches=len(log), lib_launches=int(launches), e2e_ms=float(e2e[0]), loss=float(loss_host),
+                clocks=clk.summary() if clk else None)
+
+
 def run_b200(args):
     import torch
     import torch.distributed as dist
@@ -232,7 +363,6 @@ def run_b200(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300), pg_options=opts)
 
     from memintelli_flash_b200 import DPETensor
-    from memintelli_flash_b200 import _native as N
     from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
 
     # dp x tp: ranks form dp groups of tp consecutive ranks; a group shards every crossbar across its tp
@@ -250,94 +380,72 @@ def run_b200(args):
     model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=tp_group)
     torch.cuda.synchronize()
     g = torch.Generator().manual_seed(1)
-    ids_host = torch.randint(0, ARCH["vocab"], (BATCH, SEQ), generator=g).pin_memory()
-    ids_host = ids_host[s0:s1]                    # this dp group's sequences
-    ids = ids_host.to(dev)
+    ids_all = torch.randint(0, ARCH["vocab"], (BATCH, SEQ), generator=g).pin_memory()
+    head = Layout(model, ids_all[s0:s1], dev, world, tp)
+    r = time_layout(head, engine, args, world, local, dev, clocks=True)
 
-    def step(x):
-        """One prefill step: the group's mean loss, averaged over the dp groups."""
-        loss = model(x)
-        if world > 1:
-            loss = loss.reshape(1)
-            dist.all_reduce(loss)              # tp ranks hold the same loss: the sum / world is the dp mean
-            loss = loss[0] / world
-        return loss
+    # the fully sharded layout (every crossbar over all ranks) and the layout check, at N > 1
+    tp_line = None
+    if world > 1 and tp != world and not args.no_tp_compare:
+        model_tp = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=None)
+        full = Layout(model_tp, ids_all, dev, world, world)
+        rt = time_layout(full, engine, args, world, local, dev)
+        # noise-free, both layouts compute the same losses up to fp32 summation order
+        saved = engine.read_variation
+        engine.read_variation = {i: 0.0 for i in range(engine.g_level)}
+        loss_head = float(head.step(head.ids))
+        loss_full = float(full.step(full.ids))
+        engine.read_variation = saved
+        tp_line = {"value": BATCH * SEQ * args.steps / (rt["ms"] / 1000.0), "unit": "tokens/s",
+                   "parallelism": f"dp1xtp{world}", "ms_per_step": rt["ms"] / args.steps,
+                   "e2e": BATCH * SEQ * args.steps / (rt["e2e_ms"] / 1000.0),
+                   "mvm_share": rt["mvm_ms"] / rt["ms"] if rt["ms"] else None}
+        layout_check = {"noise_free_loss": {f"dp{dp}xtp{tp}": loss_head, f"dp1xtp{world}": loss_full},
+                        "rel_diff": abs(loss_head - loss_full) / abs(loss_full)}
+        del model_tp, full
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    for _ in range(args.warmup):
-        step(ids)
-    barrier()
-    # ---- device-resident timed region
-    engine.launch_log = []
-    launches0 = N.launch_count()
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        barrier()
-        t_start.record()
-        for _ in range(args.steps):
-            loss = step(ids)
-        t_end.record()
-        barrier()
-    launches = N.launch_count() - launches0
-    ms = t_start.elapsed_time(t_end)
-    log = engine.launch_log
-    engine.launch_log = None
-    mvm_ms = sum(a.elapsed_time(b) for a, b, _, _ in log)
-    mvm_ops = sum(o for _, _, o, _ in log)
-    mvm_adc = sum(e for _, _, _, e in log)
-    ms_t = torch.tensor([ms, mvm_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms, mvm_ms_max = float(ms_t[0]), float(ms_t[1])
+    ms = r["ms"]
     tokens = BATCH * SEQ * args.steps
     value = tokens / (ms / 1000.0)
-    # ---- end to end through the public API: host ids in, host loss out, every step
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        loss_host = step(ids_host.to(dev, non_blocking=True)).item()
-    e1.record()
-    barrier()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-    e2e_value = tokens / (float(e2e_ms[0]) / 1000.0)
-
     peaks, peak_kind = load_peaks()
-    achieved = mvm_ops / (mvm_ms / 1000.0) / 1e12 if mvm_ms > 0 else 0.0
+    mvm_ms = r["mvm_ms"]
+    achieved = r["mvm_ops"] / (mvm_ms / 1000.0) / 1e12 if mvm_ms > 0 else 0.0
     peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
-    clocks = clk.summary()
+    clocks = r["clocks"]
     sm_clock = clocks["sm_mhz"] or 1965.0
-    epi_ceiling = 148 * 64 * sm_clock * 1e6 / 1e12   # ADC events (T/s) at 2 issue slots per event
+    epi_ceiling = 148 * (64.0 / MVM_FMAHEAVY_OPS_PER_ADC_EVENT) * sm_clock * 1e6   # ADC events / s
+    adc_rate = r["mvm_adc"] / (mvm_ms / 1000.0) if mvm_ms else 0.0
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+                "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
+                "data": "synthetic",
                 "config": dict(base_config(), parallelism=f"dp{dp}xtp{tp}" if world > 1 else "single",
                                l2="inputs larger than L2 (3 GB of programmed crossbars per forward)"),
-                "sliced_mvm_tops": ops_per_token() * BATCH * SEQ * args.steps / (ms / 1000.0) / 1e12,
+                "sliced_mvm_tops": ops_per_token() * tokens / (ms / 1000.0) / 1e12,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                             "frac": achieved / peak, "traffic": None, "peak_kind": f"bf16 sustained ({peak_kind})",
-                             "kernel": "mvm_kernel (fused crossbar MVM)", "launches": len(log),
+                             "frac": achieved / peak,
+                             "traffic": MVM_DRAM_BYTES_PER_ADC_EVENT * r["mvm_adc"] / max(r["launches"], 1),
+                             "peak_kind": f"bf16 sustained ({peak_kind})",
+                             "kernel": "mvm_kernel (fused crossbar MVM)", "launches": r["launches"],
                              "kernel_share": mvm_ms / ms if ms else None,
-                             "epilogue": {"adc_events_per_s": mvm_adc / (mvm_ms / 1000.0) if mvm_ms else 0.0,
-                                          "ceiling_per_s": epi_ceiling * 1e12,
-                                          "frac": (mvm_adc / (mvm_ms / 1000.0)) / (epi_ceiling * 1e12)
-                                          if mvm_ms else 0.0}},
-                "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * SEQ * 8,
+                             "epilogue": {"adc_events_per_s": adc_rate, "ceiling_per_s": epi_ceiling,
+                                          "frac": adc_rate / epi_ceiling,
+                                          "ceiling": "FMA-heavy pipe, "
+                                                     f"{MVM_FMAHEAVY_OPS_PER_ADC_EVENT} lane ops per ADC event"}},
+                "e2e": {"value": tokens / (r["e2e_ms"] / 1000.0), "unit": "tokens/s",
+                        "h2d_bytes_per_step": (s1 - s0) * SEQ * 8 * world,      # every rank copies its ids
                         "d2h_bytes_per_step": 4},
-                "gpu_launches": int(launches),
+                "gpu_launches": r["lib_launches"],
                 "clocks": {k: clocks[k] for k in ("sm_mhz", "sm_max_mhz", "reasons")},
-                "loss": float(loss_host)}
+                "loss": r["loss"]}
+        if tp_line is not None:
+            line["tp"] = tp_line
+            line["layout_check"] = layout_check
         if not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
-    del model
+    del model, head
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -350,6 +458,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp-compare", action="store_true",
+                    help="at N > 1, skip the fully sharded layout's measurement and the layout check")
     ap.add_argument("--tp", type=int, default=0,
                     help="ranks per crossbar-sharding group (0: pure data parallel when the batch divides by the "
                          "rank count, else all ranks shard)")

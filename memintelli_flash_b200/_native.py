@@ -145,6 +145,30 @@ def stream_ptr(device=None):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+class _NoGuard:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+
+_NO_GUARD = _NoGuard()
+
+
+def device_guard(device):
+    """Context that makes ``device`` the current CUDA device for the native calls inside it.
+
+    The library launches on the current device (and sets per-device kernel attributes there), so
+    a call whose buffers live on another device must switch to it first.  Returns a no-op context
+    when ``device`` is already current, which keeps the per-layer host path cheap."""
+    import torch
+    idx = device.index if isinstance(device, torch.device) else device
+    if idx is None or idx == torch.cuda.current_device():
+        return _NO_GUARD
+    return torch.cuda.device(idx)
+
+
 def launch_count() -> int:
     """Kernels launched by the native library so far in this process."""
     return int(lib().mib_launch_count())

@@ -53,6 +53,11 @@ class _ShardBase(torch.nn.Module):
         self.group = group
         world, rank = (1, 0) if presharded else _world(group)
         out_f, in_f = weight.shape
+        if world > 1 and (isinstance(weight_quant_gran, str) or (dim == 1 and isinstance(input_quant_gran, str))):
+            # a per-matrix / per-row / per-column scale spans every shard: each rank would compute its own
+            # maximum over its part only, and the shards would no longer add up to the unsharded layer
+            raise ValueError("crossbar sharding needs tuple quant_gran blocks; a string granularity "
+                             f"({weight_quant_gran!r} / {input_quant_gran!r}) makes one scale span all shards")
         qg = weight_quant_gran if not isinstance(weight_quant_gran, str) else (in_f, out_f)
         if dim == 0:   # output columns of W^T == rows of the (out, in) weight
             blk = math.ceil(qg[1] / weight_paral_size[1]) * weight_paral_size[1]
@@ -70,6 +75,10 @@ class _ShardBase(torch.nn.Module):
             b_local = None
             lin_in, lin_out = hi - lo, out_f
             self.full_bias = None if bias is None else bias.detach().clone()
+        if hi <= lo:
+            what = "output columns" if dim == 0 else "input rows"
+            raise ValueError(f"rank {rank} of {world} gets an empty crossbar shard: {out_f if dim == 0 else in_f} "
+                             f"{what} in blocks of {blk} do not give every rank a block")
         self.lo, self.hi, self.world, self.rank = lo, hi, world, rank
         self.in_features, self.out_features = in_f, out_f
         self.local = _LinearFromWeight(engine, w_local, b_local, input_slice, weight_slice, bw_e, input_paral_size,

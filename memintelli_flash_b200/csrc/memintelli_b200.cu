@@ -207,9 +207,27 @@ int radc_of(const mib_device_spec* d, int j, int Sy, long long* out) {
   return MIB_OK;
 }
 
+// Checks every quantity the ADC plan divides by or loops over, with the reference's messages
+// (memmat_tensor.py:98-111, 284-285), so that every entry point reaching adc_plan (mib_mvm,
+// mib_adc_plan, mib_mvm_workspace, mib_mvm_static_scratch) rejects them the same way.
+int check_engine(const SliceTab& tw, const mib_k_geom* kg, const mib_device_spec* dev) {
+  if (!kg || !dev) return fail(MIB_ERR_PARAM, "NULL argument");
+  if (kg->p < 1) return fail(MIB_ERR_PARAM, "crossbar tile depth must be positive");
+  if (kg->kt < 1) return fail(MIB_ERR_SHAPE, "K geometry has no crossbar tile");
+  if (dev->rdac < 2) return fail(MIB_ERR_PARAM, "The resolution of the DAC should be larger than 1!");
+  if (dev->g_level < 2) return fail(MIB_ERR_PARAM, "The number of the conductance levels should be larger than 1!");
+  if (dev->n_radc < 1 || dev->n_radc > MIB_MAX_SLICES) return fail(MIB_ERR_PARAM, "radc list length must be in [1, 8]");
+  if (dev->n_read_sigma < 0 || dev->n_read_sigma > MIB_MAX_LEVELS)
+    return fail(MIB_ERR_PARAM, "read variation list length must be in [0, 256]");
+  for (int j = 0; j < tw.S; ++j)
+    if (tw.maxes[j] > dev->g_level - 1) return fail(MIB_ERR_PARAM, "The weight data is out of the range!");
+  return MIB_OK;
+}
+
 // Chooses the ADC code source and the accumulation for one MVM configuration.
 int adc_plan(const SliceTab& tx, const SliceTab& tw, const mib_slice_spec* xs, const mib_slice_spec* wsp,
              const mib_k_geom* kg, const mib_device_spec* dev, AdcPlan& pl) {
+  if (int r = check_engine(tw, kg, dev)) return r;
   const long long D = static_cast<long long>(dev->rdac - 1) * (dev->g_level - 1) * kg->p;
   pl.D = D;
   bool uniform = true;

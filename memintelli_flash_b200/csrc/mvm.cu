@@ -21,6 +21,8 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <atomic>
+
 namespace mib {
 
 namespace {
@@ -350,11 +352,18 @@ template <int KIND, int MODE, int SY, bool SPLIT, int SXC>
 cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, size_t smem,
                        cudaStream_t stream) {
   auto fn = mvm_kernel<KIND, MODE, SY, SPLIT, SXC>;
-  static bool configured = false;  // per template instance; the smem cap is the same for every call
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  // The shared-memory cap is a per-device function attribute: raise it once on every device this
+  // template instance runs on (one bit per device index, set after the attribute call succeeded).
+  static std::atomic<uint64_t> configured[2] = {};
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return e;
+  if (device < 0 || device >= 128) return cudaErrorInvalidDevice;
+  const uint64_t bit = uint64_t(1) << (device & 63);
+  if (!(configured[device >> 6].load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    configured = true;
+    configured[device >> 6].fetch_or(bit, std::memory_order_release);
   }
   constexpr int CG = column_groups(SY);
   constexpr int BN = 16 * CG;

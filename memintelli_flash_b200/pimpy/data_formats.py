@@ -181,12 +181,13 @@ class SlicedData(object):
             data = data.float()
         self._cache = {}
         self._overrides = {}
-        if self.is_weight:
-            if data.dim() != 2:
-                raise ValueError('The weight data must be 2-D!')
-            engine._program_weight(self, data)
-        else:
-            engine._slice_input(self, data)
+        with N.device_guard(data.device):
+            if self.is_weight:
+                if data.dim() != 2:
+                    raise ValueError('The weight data must be 2-D!')
+                engine._program_weight(self, data)
+            else:
+                engine._slice_input(self, data)
         self.shape = data.shape
 
     def _slice_conv_imp(self, engine, x, kernel_size, stride, padding, dilation):
@@ -198,7 +199,8 @@ class SlicedData(object):
             x = x.float()
         self._cache = {}
         self._overrides = {}
-        engine._slice_conv_input(self, x, kernel_size, stride, padding, dilation)
+        with N.device_guard(x.device):
+            engine._slice_conv_input(self, x, kernel_size, stride, padding, dilation)
 
     # ------------------------------------------------- reference-layout views
     def _get(self, name, fn):

@@ -182,11 +182,12 @@ class DPETensor(object):
         kind = self.operand_kind
         pkind = self._input_plane_kind(kind)
         geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
-        try:
-            self._run_input_slicing(sd, kind, geom, qg, B, T, K, squeeze,
-                                    lambda spec, kg, bufs: launch(spec, kg, pkind, bufs), pkind)
-        except NotImplementedError:
-            self._slice_input(sd, fallback().float())
+        with N.device_guard(self.device):
+            try:
+                self._run_input_slicing(sd, kind, geom, qg, B, T, K, squeeze,
+                                        lambda spec, kg, bufs: launch(spec, kg, pkind, bufs), pkind)
+            except NotImplementedError:
+                self._slice_input(sd, fallback().float())
         sd.shape = torch.Size(shape)
 
     @staticmethod
@@ -325,7 +326,10 @@ class DPETensor(object):
         self._validate_radc_with_slices(mat)
         if self.wire_resistance > 0:
             raise NotImplementedError('The wire_factor is not supported in the training version!')
-        return self._mvm(x, mat, out=out, bias=bias, layout=layout, acc_dump=acc_dump)
+        if x._buf is None:
+            raise ValueError('slice_data_imp must be called on both operands first')
+        with N.device_guard(x._buf["planes"].device):
+            return self._mvm(x, mat, out=out, bias=bias, layout=layout, acc_dump=acc_dump)
 
     def _plan(self, xs: N.SliceSpec, ws: N.SliceSpec, kg: N.KGeom, dspec: N.DeviceSpec, device):
         key = (bytes(xs), bytes(ws), bytes(kg), bytes(dspec), str(device))

@@ -65,11 +65,13 @@ def rms_norm(x, w, eps):
 
 
 def rope_cache(T, dim, theta, device):
-    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, device=device, dtype=torch.float64) / dim))
-    t = torch.arange(T, device=device, dtype=torch.float64)
+    """(T, dim) cos / sin tables of the default rotary embedding, in float32 as the Hugging Face Qwen3
+    model evaluates them (inverse frequencies and position x frequency products in fp32)."""
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.int64).float() / dim))
+    t = torch.arange(T, dtype=torch.int64).float()
     f = torch.outer(t, inv)
     emb = torch.cat([f, f], dim=-1)
-    return emb.cos().float(), emb.sin().float()
+    return emb.cos().to(device), emb.sin().to(device)
 
 
 def apply_rope(x, cos, sin):
@@ -79,14 +81,30 @@ def apply_rope(x, cos, sin):
 
 
 class Qwen3CimLayer(torch.nn.Module):
-    def __init__(self, arch: Qwen3Arch, engine, spec: CimSpec, gen: torch.Generator, device, group=None):
+    def __init__(self, arch: Qwen3Arch, engine, spec: CimSpec, gen: torch.Generator, device, group=None,
+                 weights=None, prefix=""):
         super().__init__()
         a = arch
         self.arch = a
         std = 0.02
+        names = iter(("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                      "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"))
 
         def w(o, i):
+            """The next linear's (out, in) weight: from ``weights`` (Hugging Face Qwen3 names) when given,
+            else random (std 0.02, drawn in this order)."""
+            name = next(names)
+            if weights is not None:
+                t = weights[f"{prefix}{name}.weight"]
+                if tuple(t.shape) != (o, i):
+                    raise ValueError(f"{prefix}{name}.weight has shape {tuple(t.shape)}, expected {(o, i)}")
+                return t.to(device=device, dtype=torch.float32)
             return torch.randn(o, i, generator=gen, device=device) * std
+
+        def norm(name, n):
+            if weights is None:
+                return torch.ones(n, device=device)
+            return weights[f"{prefix}{name}.weight"].to(device=device, dtype=torch.float32).reshape(n)
 
         kw = dict(group=group, device=device, **spec.kwargs())
         sl = (spec.input_slice, spec.weight_slice)
@@ -100,10 +118,13 @@ class Qwen3CimLayer(torch.nn.Module):
         self.gate_up_proj = ColumnShardedLinearMem(
             engine, [w(a.intermediate, a.hidden), w(a.intermediate, a.hidden)], None, *sl, **kw)
         self.down_proj = RowShardedLinearMem(engine, w(a.hidden, a.intermediate), None, *sl, **kw)
-        self.in_norm = torch.nn.Parameter(torch.ones(a.hidden, device=device), requires_grad=False)
-        self.post_norm = torch.nn.Parameter(torch.ones(a.hidden, device=device), requires_grad=False)
-        self.q_norm = torch.nn.Parameter(torch.ones(a.head_dim, device=device), requires_grad=False)
-        self.k_norm = torch.nn.Parameter(torch.ones(a.head_dim, device=device), requires_grad=False)
+        self.in_norm = torch.nn.Parameter(norm("input_layernorm", a.hidden), requires_grad=False)
+        self.post_norm = torch.nn.Parameter(norm("post_attention_layernorm", a.hidden), requires_grad=False)
+        self.q_norm = torch.nn.Parameter(norm("self_attn.q_norm", a.head_dim), requires_grad=False)
+        self.k_norm = torch.nn.Parameter(norm("self_attn.k_norm", a.head_dim), requires_grad=False)
+        # attention arithmetic: bf16 (q/k norm, RoPE and casts in mib_qk_norm_rope_bf16, then bf16 SDPA) or
+        # float32 (the same steps in torch, fp32 SDPA: the reference model's eager fp32 attention)
+        self.attn_dtype = torch.bfloat16
         q_cols, k_cols, v_cols = self.qkv_proj.split_sizes
         if q_cols % a.head_dim or k_cols % a.head_dim or k_cols == 0 or q_cols == 0:
             raise ValueError(f"crossbar sharding must give every rank whole, non-empty heads "
@@ -134,13 +155,22 @@ class Qwen3CimLayer(torch.nn.Module):
         xs = self.qkv_proj.new_input()
         self.engine.slice_rmsnorm_input(xs, h, self.in_norm, a.eps)
         qkv = self.qkv_proj.forward_sliced(xs)
-        # q/k RMSNorm, rotary embedding and bf16 casts in one pass (mib_qk_norm_rope_bf16); the torch
-        # form is rope(rms_norm(q, q_norm)) etc. (rms_norm, apply_rope above)
-        q, k, v = (torch.empty(B, T, n, a.head_dim, dtype=torch.bfloat16, device=h.device)
-                   for n in (self.local_heads, self.local_kv, self.local_kv))
-        N.call("mib_qk_norm_rope_bf16", N.ptr(qkv), B * T, qkv.stride(-2), T, self.local_heads, self.local_kv,
-               a.head_dim, N.ptr(self.q_norm), N.ptr(self.k_norm), float(a.eps), N.ptr(cos), N.ptr(sin), N.ptr(q),
-               N.ptr(k), N.ptr(v), N.stream_ptr(h.device))
+        if self.attn_dtype == torch.float32:
+            nq, nk = self.local_heads * a.head_dim, self.local_kv * a.head_dim
+            q = qkv[..., :nq].reshape(B, T, self.local_heads, a.head_dim)
+            k = qkv[..., nq:nq + nk].reshape(B, T, self.local_kv, a.head_dim)
+            v = qkv[..., nq + nk:nq + 2 * nk].reshape(B, T, self.local_kv, a.head_dim)
+            c, s_ = cos[:, None, :], sin[:, None, :]
+            q = apply_rope(rms_norm(q, self.q_norm, a.eps), c, s_)
+            k = apply_rope(rms_norm(k, self.k_norm, a.eps), c, s_)
+        else:
+            # q/k RMSNorm, rotary embedding and bf16 casts in one pass (mib_qk_norm_rope_bf16); the torch
+            # form is the float32 branch above
+            q, k, v = (torch.empty(B, T, n, a.head_dim, dtype=torch.bfloat16, device=h.device)
+                       for n in (self.local_heads, self.local_kv, self.local_kv))
+            N.call("mib_qk_norm_rope_bf16", N.ptr(qkv), B * T, qkv.stride(-2), T, self.local_heads, self.local_kv,
+                   a.head_dim, N.ptr(self.q_norm), N.ptr(self.k_norm), float(a.eps), N.ptr(cos), N.ptr(sin),
+                   N.ptr(q), N.ptr(k), N.ptr(v), N.stream_ptr(h.device))
         o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), is_causal=True,
                                            enable_gqa=self.local_heads != self.local_kv)
         o = o.transpose(1, 2).reshape(B, T, self.local_heads * a.head_dim).float()
@@ -162,7 +192,10 @@ class Qwen3CimPrefill(torch.nn.Module):
     """Random-init Qwen3-architecture model; ``forward(ids)`` returns the mean next-token loss."""
 
     def __init__(self, engine, arch: Qwen3Arch = Qwen3Arch(), spec: CimSpec = CimSpec(), seed: int = 0,
-                 device=None, group=None):
+                 device=None, group=None, weights=None):
+        """``weights``: optional state dict in Hugging Face Qwen3 naming (``model.embed_tokens.weight``,
+        ``model.layers.{i}.self_attn.q_proj.weight``, ..., ``model.norm.weight``, ``lm_head.weight``), the
+        checkpoint the reference loads (memintelli/NN_models/Qwen3.py:136-140); random init otherwise."""
         super().__init__()
         device = device or engine.device
         self.arch, self.group, self.engine = arch, group, engine
@@ -173,12 +206,19 @@ class Qwen3CimPrefill(torch.nn.Module):
         self.rank = dist.get_rank(group) if self.world > 1 else 0
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
-        self.embed = torch.nn.Parameter(torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02,
-                                        requires_grad=False)
+        if weights is None:
+            embed = torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02
+        else:
+            embed = weights["model.embed_tokens.weight"].to(device=device, dtype=torch.float32)
+        self.embed = torch.nn.Parameter(embed, requires_grad=False)
         self.layers = torch.nn.ModuleList(
-            Qwen3CimLayer(arch, engine, spec, gen, device, group) for _ in range(arch.layers))
-        self.norm = torch.nn.Parameter(torch.ones(arch.hidden, device=device), requires_grad=False)
-        w_head = torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02
+            Qwen3CimLayer(arch, engine, spec, gen, device, group, weights, f"model.layers.{i}.")
+            for i in range(arch.layers))
+        norm = torch.ones(arch.hidden, device=device) if weights is None else \
+            weights["model.norm.weight"].to(device=device, dtype=torch.float32)
+        self.norm = torch.nn.Parameter(norm, requires_grad=False)
+        w_head = torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02 if weights is None else \
+            weights["lm_head.weight"].to(device=device, dtype=torch.float32)
         self.lm_head = ColumnShardedLinearMem(engine, w_head, None, spec.input_slice, spec.weight_slice,
                                               group=group, device=device, **spec.kwargs())
         del w_head
@@ -190,8 +230,12 @@ class Qwen3CimPrefill(torch.nn.Module):
                 yield getattr(layer, name).local
         yield self.lm_head.local
 
-    @torch.no_grad()
-    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+    def set_attention_dtype(self, dtype):
+        """bf16 attention (default; the benchmark's) or float32 (the reference model's eager attention)."""
+        for layer in self.layers:
+            layer.attn_dtype = dtype
+
+    def _hidden(self, ids):
         a = self.arch
         B, T = ids.shape
         if T not in self._rope:
@@ -199,15 +243,27 @@ class Qwen3CimPrefill(torch.nn.Module):
         cos, sin = self._rope[T]                             # (T, head_dim) each
         h = F.embedding(ids, self.embed)
         if self.world > 1 and self.micro_batches > 1 and B >= self.micro_batches:
-            h = self._layers_overlapped(h, cos, sin)
-        else:
-            for layer in self.layers:
-                h = layer(h, cos, sin)
+            return self._layers_overlapped(h, cos, sin)
+        for layer in self.layers:
+            h = layer(h, cos, sin)
+        return h
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        h = self._hidden(ids)
         xs = self.lm_head.new_input()
-        self.engine.slice_rmsnorm_input(xs, h[:, :-1], self.norm, a.eps)
+        self.engine.slice_rmsnorm_input(xs, h[:, :-1], self.norm, self.arch.eps)
         logits = self.lm_head.forward_sliced(xs)             # (B, T-1, V_local)
         target = ids[:, 1:]
         return self._sharded_ce(logits, target)
+
+    @torch.no_grad()
+    def logits(self, ids: torch.Tensor) -> torch.Tensor:
+        """(B, T, V_local) logits of every position (this rank's vocabulary columns)."""
+        h = self._hidden(ids)
+        xs = self.lm_head.new_input()
+        self.engine.slice_rmsnorm_input(xs, h, self.norm, self.arch.eps)
+        return self.lm_head.forward_sliced(xs)
 
     def _layers_overlapped(self, h, cos, sin):
         """The decoder layers over ``micro_batches`` groups of sequences, with every o/down all-reduce

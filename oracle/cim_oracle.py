@@ -491,44 +491,85 @@ def ABSE(ytest, ypred):
     return np.sum(np.abs((ytest - ypred) / ytest)) / (ytest.shape[0] * ytest.shape[1])
 
 
-def mvm_float_torch(x: Sliced, w: Sliced, eng: Engine, seed: int = 0, noisy: bool = True):
-    """torch-CPU restatement of ``_dot_inference`` (memmat_tensor.py:260-409) for CPU timing.
+def mvm_float_torch(x: Sliced, w: Sliced, eng: Engine, seed: int = 0, noisy: bool = True, device="cpu",
+                    m_chunk: int = 0):
+    """torch restatement of ``_dot_inference`` (memmat_tensor.py:260-409) for timing the reference's
+    algorithm: on the CPU (its own CPU path) or on a CUDA device (its GPU path).
 
-    Same arithmetic as ``mvm_float`` in fp32 with torch's multi-threaded CPU
-    kernels (one batched contraction per slice pair, ADC, shift-add, block
-    rescale, K-tile sum), i.e. the structure and speed class of the
-    reference's own CPU path.  Read variation is drawn from a seeded torch
-    generator; stuck-at and write variation are not modelled here.
+    Same arithmetic as ``mvm_float`` in fp32 with torch kernels, in the reference's structure: one
+    batched contraction per slice pair into a (Kt, M, Np) partial tensor, ADC, shift-add, block
+    rescale, K-tile sum.  Read variation is drawn from a seeded torch generator; stuck-at and write
+    variation are not modelled here.  ``m_chunk`` > 0 processes the rows in chunks, as the reference's
+    GPU path must for large outputs (the partial of one slice pair is Kt x M x Np fp32).
+    Returns a float64 numpy array after synchronising the device.
     """
+    if m_chunk and x.squeeze and x.geom.qg0 == 1 and x.batch == 1:
+        rows = x.geom.rows_p
+        parts = [mvm_float_torch(_row_slice(x, m0, min(rows, m0 + m_chunk)), w, eng, seed + m0, noisy, device, 0)
+                 for m0 in range(0, rows, m_chunk)]
+        return np.concatenate(parts, axis=0)
+    y = torch_port_mvm(torch_port_operands(x, w, eng, device), eng, seed, noisy)
+    return _crop(y.double().cpu().numpy(), x, w)
+
+
+def torch_port_operands(x: Sliced, w: Sliced, eng: Engine, device="cpu") -> dict:
+    """Device tensors the reference's ``_dot_inference`` starts from: DAC levels of every input slice,
+    conductances G of every weight slice (memmat_tensor.py:160-202, 238-258) and the block scales."""
     import torch
-    gen = torch.Generator().manual_seed(seed)
+    dev = torch.device(device)
     p = x.geom.p1
-    Sx, Sw = len(x.slice_method), len(w.slice_method)
+    Sw = len(w.slice_method)
     _, _, mx, cx = slice_tables(x.slice_method)
     _, _, mw, cw = slice_tables(w.slice_method)
-    g = w.geom
     QG = (eng.HGS - eng.LGS) / (eng.g_level - 1)
-    Rj = eng.radc_list(Sw)
-    adcRef = (eng.HGS - eng.LGS) * eng.vread * p
     Kt = x.geom.cols_p // p
     G = torch.stack([torch.from_numpy(level_map(w.codes(t)[0], mw[t], eng.g_level - 1)) for t in range(Sw)])
-    G = G.float() * QG + eng.LGS                                              # (Sw, Kp, Np)
+    G = G.to(dev).float() * QG + eng.LGS                                      # (Sw, Kp, Np)
+    A = [torch.from_numpy(level_map(x.codes(i), mx[i], eng.rdac - 1).reshape(-1, Kt, p)).to(dev).float()
+         for i in range(len(x.slice_method))]
+    sx = torch.from_numpy(np.repeat(x.tile_scale().reshape(-1, Kt), x.geom.p0, axis=0)).to(dev).float()
+    sw = torch.from_numpy(np.repeat(w.tile_scale()[0], w.geom.p1, axis=1)).to(dev).float()
+    return dict(G=G, A=A, sx=sx, sw=sw, p=p, Kt=Kt, Np=w.geom.cols_p, mx=mx, cx=cx, mw=mw, cw=cw, dev=dev)
+
+
+def torch_port_mvm(ops: dict, eng: Engine, seed: int = 0, noisy: bool = True):
+    """The device work of one ``_dot_inference`` call (memmat_tensor.py:280-404) on prepared operands:
+    read noise on G, then for every slice pair the crossbar contraction, ADC rounding and shift-add,
+    then the block rescale and the K-tile sum.  Returns the (rows_p, Np) fp32 device tensor."""
+    import torch
+    dev, p, Kt = ops["dev"], ops["p"], ops["Kt"]
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    G = ops["G"]
+    Sw = G.shape[0]
+    Rj = eng.radc_list(Sw)
+    adcRef = (eng.HGS - eng.LGS) * eng.vread * p
     sig = eng.read_sigma()
     if noisy and sig[0] > 0:
-        G = G * torch.exp(torch.randn(G.shape, generator=gen) * sig[0])
-    Gs = (G - eng.LGS).reshape(Sw, Kt, p, g.cols_p)
+        G = G * torch.exp(torch.randn(G.shape, generator=gen, device=dev) * sig[0])
+    Gs = (G - eng.LGS).reshape(Sw, Kt, p, ops["Np"])
     out = None
-    for i in range(Sx):
-        A = torch.from_numpy(level_map(x.codes(i), mx[i], eng.rdac - 1).reshape(-1, Kt, p)).float()
+    for i, A in enumerate(ops["A"]):
         V = (eng.vread * A / (eng.rdac - 1)).transpose(0, 1)                   # (Kt, M, p)
         if noisy and eng.vnoise > 0:
-            V = V * (1 + torch.randn(V.shape, generator=gen) * eng.vnoise)
+            V = V * (1 + torch.randn(V.shape, generator=gen, device=dev) * eng.vnoise)
         for j in range(Sw):
             P = torch.bmm(V, Gs[j])                                           # (Kt, M, Np)
             P = torch.round(P / adcRef * (Rj[j] - 1)) / (Rj[j] - 1)
-            P = P * float(mx[i] * mw[j] * p * cx[i] * cw[j])
+            P = P * float(ops["mx"][i] * ops["mw"][j] * p * ops["cx"][i] * ops["cw"][j])
             out = P if out is None else out.add_(P)
-    sx = torch.from_numpy(np.repeat(x.tile_scale().reshape(-1, Kt), x.geom.p0, axis=0)).float()
-    sw = torch.from_numpy(np.repeat(w.tile_scale()[0], w.geom.p1, axis=1)).float()
-    y = (out * sx.T[:, :, None] * sw[:, None, :]).sum(0)
-    return _crop(y.double().numpy(), x, w)
+    return (out * ops["sx"].T[:, :, None] * ops["sw"][:, None, :]).sum(0)
+
+
+def _row_slice(x: Sliced, m0: int, m1: int) -> Sliced:
+    """Rows [m0, m1) of a 2-D input with one-row quant blocks (rows are independent)."""
+    import copy
+    g = x.geom
+    if g.qg0 != 1:
+        raise ValueError("row chunks need one-row input quant blocks")
+    y = copy.copy(x)
+    y.q = x.q[:, m0:m1]
+    y.bmax = x.bmax[:, m0:m1]
+    y.ebias = None if x.ebias is None else x.ebias[:, m0:m1]
+    y.deq = x.deq[:, m0:m1]
+    y.geom = Geometry(m1 - m0, g.cols, g.p0, g.p1, g.qg0, g.qg1, m1 - m0, g.nbc)
+    return y

@@ -1,13 +1,21 @@
 """Generate golden fixtures by running the reference Memintelli package on CPU.
 
-Run in a container where the reference source tree is available:
+Run where the reference source tree is available (``--ref`` or the
+MEMINTELLI_REFERENCE environment variable names it):
 
-    python tests/golden/make_golden.py --ref /root/reference [--seeds 256]
+    python tests/golden/make_golden.py --ref <reference tree> [--seeds 256] [--only PART ...]
 
-It writes ``tests/golden/cases.npz`` (deterministic noise-free cases: inputs or
-their seed, the reference's packed slice codes, block maxima / exponents and
-fp32 outputs) and ``tests/golden/noise_stats.json`` (per-seed SNR and error
-moments of the reference's noisy path, for statistical parity).
+It writes
+* ``tests/golden/cases.npz`` (deterministic noise-free cases: inputs or their
+  seed, the reference's packed slice codes, block maxima / exponents and fp32
+  outputs; part ``cases``);
+* ``tests/golden/noise_stats.json`` (per-seed SNR and error moments of the
+  reference's noisy path, for statistical parity; parts ``stats-int``,
+  ``stats-fp``, ``stats-read-k1024`` and ``stats-per-level``, merged into the
+  existing file when only some are generated);
+* ``tests/golden/qwen3_model.npz`` (logits and loss of a small Qwen3 built the
+  reference's way, ``transformers`` Qwen3ForCausalLM with every nn.Linear
+  swapped for LinearMem; part ``qwen3``).
 
 The reference imports matplotlib at module level; it is stubbed because only
 the arithmetic is exercised.
@@ -241,40 +249,60 @@ def run_layer_case(name, spec, DPETensor, LinearMem, Conv2dMem):
     return out
 
 
-def exact_nf(x, w, bw_e):
-    """Exact noise-free restatement (oracle) of the config-0 matmul with the fixed stuck-at mask."""
+def exact_nf(x, w, bw_e, stuck_rate=0.001):
+    """Exact noise-free restatement (oracle) of a matmul with the config-0 slicing and, when
+    ``stuck_rate`` > 0, the reference's fixed-seed stuck-at mask."""
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     from oracle import cim_oracle as O
     xs = O.slice_matrix(x.numpy(), [1, 1, 2, 2, 2], bw_e, (1, 32), (1, 128))
     ws = O.slice_matrix(w.numpy(), [1, 1, 2, 2, 2], bw_e, (32, 32), (128, 128))
-    eng = O.Engine(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, rate_stuck_HGS=0.001)
-    g = torch.Generator().manual_seed(123)
-    stuck = torch.rand((16, 20, 5, 32, 32), generator=g).numpy()
+    eng = O.Engine(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, rate_stuck_HGS=stuck_rate)
+    stuck = None
+    if stuck_rate > 0:
+        g = torch.Generator().manual_seed(123)
+        shape = (ws.geom.rows_p // 32, ws.geom.cols_p // 32, 5, 32, 32)
+        stuck = torch.rand(shape, generator=g).numpy()
     return O.mvm_exact(xs, ws, eng, O.weight_levels(ws, eng, stuck))
 
 
-def noise_stats(n_seeds, DPETensor, SlicedData):
-    """Per-seed SNR and error moments of the reference's noisy path (config 0 engine)."""
+# Noise-statistics arms: input / weight shapes, number format and the noisy device model.  Every arm
+# uses slices [1,1,2,2,2], input (1,128)/(1,32), weight (128,128)/(32,32), HGS 1e-5, LGS 1e-8, 4 levels,
+# rdac 4, radc 4096; the noise-free twin of each seed zeroes read variation and vnoise only.
+STAT_ARMS = {
+    # config 0's device model (example 1)
+    "int": dict(xs=(400, 500), ws=(500, 600), bw_e=None, stuck=0.001, read=0.05, vnoise=0.05),
+    "fp": dict(xs=(400, 500), ws=(500, 600), bw_e=8, stuck=0.001, read=0.05, vnoise=0.05),
+    # the Qwen3 example's device model (examples/11_qwen3_wikitext2_inference.py:66-77: read variation
+    # 0.05 only) at the Qwen3-0.6B hidden width
+    "read_k1024": dict(xs=(256, 1024), ws=(1024, 512), bw_e=None, stuck=0.0, read=0.05, vnoise=0.0),
+    # per-level read variation (memmat_tensor.py:226-233)
+    "per_level": dict(xs=(400, 500), ws=(500, 600), bw_e=None, stuck=0.0,
+                      read={0: 0.02, 1: 0.05, 2: 0.05, 3: 0.1}, vnoise=0.0),
+}
+
+
+def noise_stats(arms, n_seeds, DPETensor, SlicedData):
+    """Per-seed SNR and error moments of the reference's noisy path for each arm in ``arms``."""
     res = {}
-    for bw_e in (None, 8):
-        key = "fp" if bw_e else "int"
+    for key in arms:
+        a = STAT_ARMS[key]
         rows = []
         t0 = time.time()
         for s in range(n_seeds):
             g = torch.Generator().manual_seed(1000 + s)
-            x = torch.randn(400, 500, generator=g)
-            w = torch.randn(500, 600, generator=g)
+            x = torch.randn(*a["xs"], generator=g)
+            w = torch.randn(*a["ws"], generator=g)
             ideal = (x.double() @ w.double()).numpy()
             outs = []
             for noisy in (True, False):
                 kw = dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.0,
-                          rate_stuck_HGS=0.001, rate_stuck_LGS=0.0,
-                          read_variation=0.05 if noisy else 0.0, vnoise=0.05 if noisy else 0.0)
+                          rate_stuck_HGS=a["stuck"], rate_stuck_LGS=0.0,
+                          read_variation=a["read"] if noisy else 0.0, vnoise=a["vnoise"] if noisy else 0.0)
                 torch.manual_seed(50_000 + s)
                 eng = DPETensor(device=torch.device("cpu"), **kw)
-                xs = SlicedData(torch.tensor([1, 1, 2, 2, 2]), bw_e=bw_e, is_weight=False, paral_size=(1, 32),
+                xs = SlicedData(torch.tensor([1, 1, 2, 2, 2]), bw_e=a["bw_e"], is_weight=False, paral_size=(1, 32),
                                 quant_gran=(1, 128), device=torch.device("cpu"), inference=True)
-                ws = SlicedData(torch.tensor([1, 1, 2, 2, 2]), bw_e=bw_e, is_weight=True, paral_size=(32, 32),
+                ws = SlicedData(torch.tensor([1, 1, 2, 2, 2]), bw_e=a["bw_e"], is_weight=True, paral_size=(32, 32),
                                 quant_gran=(128, 128), device=torch.device("cpu"), inference=True)
                 ws.slice_data_imp(eng, w)
                 xs.slice_data_imp(eng, x)
@@ -284,7 +312,7 @@ def noise_stats(n_seeds, DPETensor, SlicedData):
             snr = 10 * np.log10(np.sum(ideal ** 2) / np.sum((ideal - yn) ** 2))
             # the reference's own noise-free output carries its fp32 tie-rounding bias; record it
             # against the exact restatement so means can be compared on one baseline
-            tie_bias = float((y0 - exact_nf(x, w, bw_e)).mean())
+            tie_bias = float((y0 - exact_nf(x, w, a["bw_e"], a["stuck"])).mean())
             rows.append([s, snr, float(e.mean()), float(e.std()), float(np.sqrt(np.mean(y0 ** 2))), tie_bias])
         res[key] = rows
         print(f"noise stats {key}: {n_seeds} seeds in {time.time() - t0:.1f}s; "
@@ -292,43 +320,141 @@ def noise_stats(n_seeds, DPETensor, SlicedData):
     return res
 
 
+def qwen3_model(Wrapper, DPETensor, replace_linear):
+    """Logits and loss of the small Qwen3 (qwen3_small.py) built the reference's way: transformers'
+    Qwen3ForCausalLM with every nn.Linear replaced by the reference's LinearMem through its own
+    _replace_linear_with_linearmem, wrapped in Qwen3MemWrapper, then update_weight() and
+    prepare_for_inference() (memintelli/NN_models/Qwen3.py:22-106); noise-free engine, fp32 eager
+    attention, on the CPU.  Two ADC resolutions: 289 (= D + 1, lossless and tie-free) and
+    4096 (the benchmark's, with half-way ties)."""
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    import qwen3_small as Q
+    from transformers import Qwen3ForCausalLM
+    sd = Q.state_dict()
+    ids = Q.token_ids()
+    out = {"ids": ids.numpy(), "weights_sum": np.array([float(sum(v.double().sum() for v in sd.values()))])}
+    for radc in (289, 4096):
+        torch.manual_seed(0)
+        model = Qwen3ForCausalLM(Q.hf_config())
+        model.load_state_dict(sd)
+        eng = DPETensor(device=torch.device("cpu"), HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=radc,
+                        **NOISE_FREE)
+        mem_args = dict(engine=eng, input_slice=[1, 1, 2, 2, 2], weight_slice=[1, 1, 2, 2, 2],
+                        device=torch.device("cpu"), bw_e=None, input_paral_size=(1, 32),
+                        weight_paral_size=(32, 32), input_quant_gran=(1, 128), weight_quant_gran=(128, 128))
+        replace_linear(model, mem_args)
+        # the reference's own flow (examples/11_qwen3_wikitext2_inference.py:100-102): program the copied
+        # weights into the crossbars, then switch every LinearMem to its inference path
+        wrapped = Wrapper(model, mem_enabled=True)
+        wrapped.update_weight()
+        wrapped.prepare_for_inference()
+        with torch.no_grad():
+            res = wrapped(input_ids=ids, labels=ids)
+        out[f"logits_r{radc}"] = res.logits.float().numpy()
+        out[f"loss_r{radc}"] = np.array([float(res.loss)])
+        # the same model with every linear on the oracle (exact, half-even ADC ties), for the tie shift
+        torch.manual_seed(0)
+        exact = Qwen3ForCausalLM(Q.hf_config())
+        exact.load_state_dict(sd)
+        _swap_oracle_linears(exact, radc)
+        exact.eval()
+        with torch.no_grad():
+            out[f"logits_oracle_r{radc}"] = exact(input_ids=ids).logits.float().numpy()
+        # the same model without crossbars, for scale
+        if radc == 289:
+            plain = Qwen3ForCausalLM(Q.hf_config())
+            plain.load_state_dict(sd)
+            plain.eval()
+            with torch.no_grad():
+                out["logits_float"] = plain(input_ids=ids).logits.float().numpy()
+        print(f"qwen3 small radc {radc}: loss {float(res.loss):.6f}")
+    return out
+
+
+class _OracleLinear(torch.nn.Module):
+    """nn.Linear replacement computing the crossbar matmul with the oracle's exact restatement."""
+
+    def __init__(self, lin, radc):
+        super().__init__()
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+        from oracle import cim_oracle as O
+        self.O = O
+        self.ws = O.slice_matrix(lin.weight.detach().t().contiguous().numpy(), [1, 1, 2, 2, 2], None, (32, 32),
+                                 (128, 128))
+        self.eng = O.Engine(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=radc)
+
+    def forward(self, x):
+        shp = x.shape
+        xs = self.O.slice_matrix(x.reshape(-1, shp[-1]).detach().float().numpy(), [1, 1, 2, 2, 2], None, (1, 32),
+                                 (1, 128))
+        y = self.O.mvm_exact(xs, self.ws, self.eng)
+        return torch.from_numpy(y.astype(np.float32)).reshape(*shp[:-1], -1)
+
+
+def _swap_oracle_linears(module, radc):
+    for name, child in list(module.named_children()):
+        if isinstance(child, torch.nn.Linear):
+            setattr(module, name, _OracleLinear(child, radc))
+        else:
+            _swap_oracle_linears(child, radc)
+
+
+PARTS = ("cases", "stats-int", "stats-fp", "stats-read-k1024", "stats-per-level", "qwen3")
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("MEMINTELLI_REFERENCE"),
+                    help="reference source tree (default: $MEMINTELLI_REFERENCE)")
     ap.add_argument("--seeds", type=int, default=256)
-    ap.add_argument("--skip-stats", action="store_true")
+    ap.add_argument("--only", nargs="*", choices=PARTS, default=list(PARTS))
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("name the reference source tree with --ref or MEMINTELLI_REFERENCE")
     _stub_matplotlib()
     sys.path.insert(0, args.ref)
     torch.set_num_threads(os.cpu_count())
     from memintelli.pimpy.memmat_tensor import DPETensor
     from memintelli.pimpy.data_formats import SlicedData
-
-    here = os.path.dirname(os.path.abspath(__file__))
-    arrays = {}
-    meta = {}
-    for name, spec in CASES.items():
-        t0 = time.time()
-        out = run_case(name, spec, DPETensor, SlicedData)
-        for k, v in out.items():
-            arrays[f"{name}/{k}"] = v
-        meta[name] = {k: v for k, v in spec.items()}
-        print(f"{name}: y {out['y'].shape} in {time.time() - t0:.2f}s")
     from memintelli.NN_layers.linear import LinearMem
     from memintelli.NN_layers.convolution import Conv2dMem
-    for name, spec in LAYER_CASES.items():
-        out = run_layer_case(name, spec, DPETensor, LinearMem, Conv2dMem)
-        for k, v in out.items():
-            arrays[f"{name}/{k}"] = v
-        meta[name] = dict(spec)
-        print(f"{name}: y {out['y'].shape}")
-    np.savez_compressed(os.path.join(here, "cases.npz"), **arrays)
-    with open(os.path.join(here, "cases.json"), "w") as f:
-        json.dump(meta, f, indent=1)
-    if not args.skip_stats:
-        st = noise_stats(args.seeds, DPETensor, SlicedData)
-        with open(os.path.join(here, "noise_stats.json"), "w") as f:
-            json.dump({"columns": ["seed", "snr_db", "err_mean", "err_std", "y_rms", "tie_bias"], **st}, f)
+
+    here = os.path.dirname(os.path.abspath(__file__))
+    if "cases" in args.only:
+        arrays = {}
+        meta = {}
+        for name, spec in CASES.items():
+            t0 = time.time()
+            out = run_case(name, spec, DPETensor, SlicedData)
+            for k, v in out.items():
+                arrays[f"{name}/{k}"] = v
+            meta[name] = {k: v for k, v in spec.items()}
+            print(f"{name}: y {out['y'].shape} in {time.time() - t0:.2f}s")
+        for name, spec in LAYER_CASES.items():
+            out = run_layer_case(name, spec, DPETensor, LinearMem, Conv2dMem)
+            for k, v in out.items():
+                arrays[f"{name}/{k}"] = v
+            meta[name] = dict(spec)
+            print(f"{name}: y {out['y'].shape}")
+        np.savez_compressed(os.path.join(here, "cases.npz"), **arrays)
+        with open(os.path.join(here, "cases.json"), "w") as f:
+            json.dump(meta, f, indent=1)
+    arms = [p[len("stats-"):].replace("-", "_") for p in args.only if p.startswith("stats-")]
+    if arms:
+        path = os.path.join(here, "noise_stats.json")
+        st = {"columns": ["seed", "snr_db", "err_mean", "err_std", "y_rms", "tie_bias"]}
+        if os.path.exists(path):
+            with open(path) as f:
+                st.update(json.load(f))
+        st.update(noise_stats(arms, args.seeds, DPETensor, SlicedData))
+        st["arms"] = {k: {kk: (vv if not isinstance(vv, dict) else {str(a): b for a, b in vv.items()})
+                          for kk, vv in STAT_ARMS[k].items()} for k in STAT_ARMS if k in st}
+        with open(path, "w") as f:
+            json.dump(st, f)
+    if "qwen3" in args.only:
+        from memintelli.NN_models.Qwen3 import Qwen3MemWrapper, _replace_linear_with_linearmem
+        out = qwen3_model(Qwen3MemWrapper, DPETensor, _replace_linear_with_linearmem)
+        np.savez_compressed(os.path.join(here, "qwen3_model.npz"), **out)
 
 
 if __name__ == "__main__":

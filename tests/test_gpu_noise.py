@@ -15,26 +15,39 @@ pytestmark = pytest.mark.gpu
 SEEDS = 256
 
 
-def _engine(M, cuda, noisy):
+def _arm(mode):
+    """Shapes, number format and noisy device model of one arm of noise_stats.json (make_golden.py)."""
+    a = dict(G.noise_stats()["arms"][mode])
+    if isinstance(a["read"], dict):
+        a["read"] = {int(k): v for k, v in a["read"].items()}
+    return a
+
+
+def _engine(M, cuda, arm, noisy):
     e = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.0,
-                    rate_stuck_HGS=0.001, rate_stuck_LGS=0.0, read_variation=0.05 if noisy else 0.0,
-                    vnoise=0.05 if noisy else 0.0)
+                    rate_stuck_HGS=arm["stuck"], rate_stuck_LGS=0.0,
+                    read_variation=arm["read"] if noisy else 0.0, vnoise=arm["vnoise"] if noisy else 0.0)
     e.fault_field_device = "cpu"
     return e
 
 
-@pytest.mark.parametrize("mode", ["int", "fp"])
+@pytest.mark.parametrize("mode", ["int", "fp", "read_k1024", "per_level"])
 def test_noise_statistics(mode, cuda):
+    """int / fp: config 0's device model (stuck-at 1e-3, read variation 0.05, voltage noise 0.05).
+    read_k1024: the benchmark's device model (read variation 0.05 only) at K = 1024, which slices inputs
+    straight into FP16 planes.  per_level: read variation {0: 0.02, 1: 0.05, 2: 0.05, 3: 0.1} by level
+    (memmat_tensor.py:226-233)."""
     import memintelli_flash_b200 as M
     ref = np.array(G.noise_stats()[mode])
-    bw_e = 8 if mode == "fp" else None
-    en, e0 = _engine(M, cuda, True), _engine(M, cuda, False)
+    arm = _arm(mode)
+    bw_e = arm["bw_e"]
+    en, e0 = _engine(M, cuda, arm, True), _engine(M, cuda, arm, False)
     sm = torch.tensor([1, 1, 2, 2, 2])
     rows = []
     for s in range(SEEDS):
         g = torch.Generator().manual_seed(1000 + s)
-        x = torch.randn(400, 500, generator=g)
-        w = torch.randn(500, 600, generator=g)
+        x = torch.randn(*arm["xs"], generator=g)
+        w = torch.randn(*arm["ws"], generator=g)
         ideal = (x.double() @ w.double()).numpy()
         outs = []
         for eng in (en, e0):
@@ -44,6 +57,8 @@ def test_noise_statistics(mode, cuda):
                               device=cuda, inference=True)
             ws.slice_data_imp(eng, w.to(cuda))
             xs.slice_data_imp(eng, x.to(cuda))
+            if eng is en and arm["vnoise"] == 0:
+                assert xs._buf["planes"].dtype == torch.float16     # the benchmark's input path
             torch.manual_seed(50_000 + s)
             outs.append(eng(xs, ws).double().cpu().numpy())
         yn, y0 = outs

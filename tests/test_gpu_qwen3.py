@@ -114,3 +114,65 @@ def test_crossbar_sharded_model_matches_single_gpu():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert abs(loss_sharded - loss_single) < 1e-5 * abs(loss_single)
+
+
+def _small_reference_model(cuda, radc):
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import qwen3_small as Q
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
+    fx = dict(np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "qwen3_model.npz")))
+    sd = Q.state_dict()
+    # the fixture was made from these exact weights
+    assert abs(float(sum(v.double().sum() for v in sd.values())) - fx["weights_sum"][0]) < 1e-6
+    eng = M.DPETensor(device=cuda, **dict(NOISE_FREE, radc=radc))
+    c = Q.CONFIG
+    arch = Qwen3Arch(hidden=c["hidden"], layers=c["layers"], heads=c["heads"], kv_heads=c["kv_heads"],
+                     head_dim=c["head_dim"], intermediate=c["intermediate"], vocab=c["vocab"],
+                     rope_theta=c["rope_theta"], eps=c["eps"])
+    model = Qwen3CimPrefill(eng, arch, device=cuda, weights=sd)
+    return model, torch.from_numpy(fx["ids"]).to(cuda), fx
+
+
+def _rel(a, b):
+    return float(np.linalg.norm(a - b) / np.linalg.norm(b))
+
+
+@pytest.mark.parametrize("radc", [289, 4096])
+def test_small_model_matches_reference_model(radc, cuda):
+    """A small Qwen3 built the reference's way (transformers Qwen3ForCausalLM, every nn.Linear swapped for
+    the reference's LinearMem, update_weight + prepare_for_inference; memintelli/NN_models/Qwen3.py:22-106),
+    run on the CPU in fp32 by tests/golden/make_golden.py, against Qwen3CimPrefill loaded with the same
+    weights, noise-free, fp32 attention.
+
+    radc 289 is lossless and tie-free: each crossbar matmul equals the reference's to fp32 rounding, and
+    the logits differ only where fp32 summation order (RMSNorm in the slicing, attention) moves an input
+    code by one step; the exact restatement of the model (every linear on the oracle) sits 6e-4 from the
+    reference there, and 5e-3 is a fifth of what the crossbars themselves change (2.2% against the float
+    model).  radc 4096 has half-way ADC ties, which the reference rounds up 62-72% of the time and this
+    library rounds half-to-even; there the oracle model sits 1.7e-2 from the reference and this model
+    must sit within 5e-3 of the oracle model."""
+    model, ids, fx = _small_reference_model(cuda, radc)
+    model.set_attention_dtype(torch.float32)
+    logits = model.logits(ids).double().cpu().numpy()
+    ref, exact = fx[f"logits_r{radc}"].astype(np.float64), fx[f"logits_oracle_r{radc}"].astype(np.float64)
+    d_exact, d_ref = _rel(logits, exact), _rel(logits, ref)
+    print(f"radc {radc}: vs oracle model {d_exact:.2e}, vs reference model {d_ref:.2e} "
+          f"(oracle vs reference {_rel(exact, ref):.2e})")
+    assert d_exact <= 5e-3
+    assert d_ref <= _rel(exact, ref) + 5e-3
+    loss = float(model(ids))
+    assert abs(loss - float(fx[f"loss_r{radc}"][0])) <= 1e-3
+
+
+def test_small_model_bf16_attention_close_to_reference(cuda):
+    """The benchmark's bf16 attention (mib_qk_norm_rope_bf16 + bf16 SDPA) against the same reference logits:
+    bf16 keeps 8 significand bits (relative step 2^-8 = 3.9e-3), so the logits may move by a few 1e-3."""
+    model, ids, fx = _small_reference_model(cuda, 289)
+    logits = model.logits(ids).double().cpu().numpy()
+    ref = fx["logits_r289"].astype(np.float64)
+    d = _rel(logits, ref)
+    print(f"bf16 attention vs reference model {d:.2e}")
+    assert d <= 2e-2
+    assert abs(float(model(ids)) - float(fx["loss_r289"][0])) <= 5e-3

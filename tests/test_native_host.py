@@ -146,3 +146,40 @@ def test_fused_producers_and_attention_prep_check_arguments_on_the_host():
     assert L.mib_qk_norm_rope_bf16(*args[:6], 96, *args[7:]) == N.MIB_ERR_UNSUPPORTED
     assert L.mib_qk_norm_rope_bf16(fake, 8, 4000, *args[3:]) == N.MIB_ERR_SHAPE
     assert L.mib_qk_norm_rope_bf16(None, *args[1:]) == N.MIB_ERR_PARAM
+
+
+def test_engine_parameters_checked_by_every_plan_entry():
+    """rdac or g_level below 2 make the ADC divisor zero: every entry point that plans an MVM returns
+    MIB_ERR_PARAM with the reference's message instead of dividing by it."""
+    L = N.lib()
+    xs, ws, kg = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 32), (128, 128)), _kg(256)
+    fake = ctypes.c_void_p(0x1000)          # never dereferenced: the calls fail their host checks
+    for bad, msg in ((_dev(4096, rdac=1), b"DAC"), (_dev(4096, g=1), b"conductance levels")):
+        rc, _, _ = _plan(xs, ws, kg, bad)
+        assert rc == N.MIB_ERR_PARAM and msg in L.mib_last_error()
+        f = N.c_i64(-1)
+        assert L.mib_mvm_workspace(64, 64, xs, ws, kg, bad, f) == N.MIB_ERR_PARAM
+        assert msg in L.mib_last_error()
+        lay = N.OutLayout(64, 0, 64, 1)
+        assert L.mib_mvm_static_scratch(fake, fake, 64, xs, fake, fake, 64, ws, kg, bad, 0, None, 0, fake, lay,
+                                        None, None) == N.MIB_ERR_PARAM
+        assert msg in L.mib_last_error()
+    bad_kg = _kg(256)
+    bad_kg.p = 0
+    rc, _, _ = _plan(xs, ws, bad_kg, _dev(4096))
+    assert rc == N.MIB_ERR_PARAM
+
+
+def test_static_scratch_rejects_oversized_split_before_any_launch():
+    """128 x 4800 outputs fill 100 of 148 SMs: the underfilled-grid split asks for two partial outputs,
+    1.23 M floats, more than the 2^20 the built-in scratch holds."""
+    L = N.lib()
+    xs, ws, kg, dev = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 32), (128, 128)), _kg(1024), _dev(4096)
+    f = N.c_i64(-1)
+    assert L.mib_mvm_workspace(128, 4800, xs, ws, kg, dev, f) == 0
+    assert f.value == 2 * 128 * 4800 > (1 << 20)
+    fake = ctypes.c_void_p(0x1000)
+    lay = N.OutLayout(128, 0, 4800, 1)
+    assert L.mib_mvm_static_scratch(fake, fake, 128, xs, fake, fake, 4800, ws, kg, dev, 0, None, 0, fake, lay,
+                                    None, None) == N.MIB_ERR_UNSUPPORTED
+    assert b"built-in scratch" in L.mib_last_error()

@@ -75,3 +75,47 @@ def test_column_and_row_shards_are_exact():
         assert p.exitcode == 0
     assert col_err == 0.0                       # column shards are bit-identical
     assert row_err <= 1e-12 * scale             # row shards: exact up to summation order
+
+
+def _reject_worker(rank, world, port, q):
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    from memintelli_flash_b200.crossbar_shard import ColumnShardedLinearMem, RowShardedLinearMem
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    errs = []
+    w = torch.zeros(256, 256)
+    cases = [
+        # a per-matrix weight scale would span both shards
+        (RowShardedLinearMem, w, dict(weight_quant_gran="per-matrix")),
+        (ColumnShardedLinearMem, w, dict(weight_quant_gran="per-matrix")),
+    ]
+    if rank == 1:   # 128 output columns in 128-column blocks leave rank 1 without a shard
+        cases.append((ColumnShardedLinearMem, torch.zeros(128, 256), dict(weight_quant_gran=(128, 128))))
+    for cls, weight, kw in cases:
+        try:
+            cls(None, weight, None, SM, SM, weight_paral_size=(32, 32), **kw)
+            errs.append(None)
+        except ValueError as e:          # raised on the host, before any crossbar is programmed
+            errs.append(str(e))
+    q.put((rank, errs))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharding_rejects_string_granularity_and_empty_shards():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_reject_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=240) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in (0, 1):
+        assert got[r][0] and "string granularity" in got[r][0]
+        assert got[r][1] and "string granularity" in got[r][1]
+    assert len(got[0]) == 2
+    assert got[1][2] and "empty crossbar shard" in got[1][2]
