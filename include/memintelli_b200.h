@@ -109,6 +109,17 @@ int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_
                          void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
                          cudaStream_t stream);
 
+/* mib_slice_conv_input with the call's voltage noise applied while the planes are written
+ * (memmat_tensor.py:297-299: V * (1 + vnoise * N(0,1)) per input element and slice, shared by all output
+ * columns).  The planes are FP16; the normals are the ones mib_input_noise(seed, call) would draw for the
+ * same plane elements, so this equals mib_slice_conv_input to E4M3 followed by mib_input_noise, bit for
+ * bit, in one pass.  For a layer that slices its input once per multiply (Conv2dMem). */
+int mib_slice_conv_input_noisy(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
+                               int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
+                               const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, void* planes_fp16,
+                               float* tile_scale, float* block_max, float* block_exp, uint8_t* packed, double vnoise,
+                               uint64_t seed, uint64_t call, cudaStream_t stream);
+
 /* Fused producers of an input (no reference counterpart).  Each slices a row transform of x with
  * the same arguments and buffers as mib_slice_input, without materialising the transformed matrix;
  * in the reference they are a torch pass followed by SlicedData.slice_data_imp.  Both need one-row
@@ -231,6 +242,15 @@ int mib_qk_norm_rope_bf16(const float* qkv, int64_t tokens, int64_t ld_token, in
 /* Reads and clears the device-side error flag of the current device (synchronises it).
  * Returns MIB_OK, or MIB_ERR_TIMEOUT when a kernel gave up a bounded wait. */
 int mib_device_status(void);
+
+/* Test hook for the failure path of the bounded device waits (no reference counterpart; the reference
+ * has no device-side waits).  Arms a one-shot flag on the calling thread: the next mib_mvm launched
+ * from it runs with its MMA warp held (it issues and commits nothing, so no accumulator ever becomes
+ * ready) and with `wait_limit_cycles` (1 .. 4e9) as the limit of its abortable mbarrier waits.  The
+ * epilogue's first wait then runs out; the kernel raises its abort flag, drains its in-flight copies,
+ * frees its tensor memory and returns, leaving that call's output undefined, and the next
+ * mib_device_status() returns MIB_ERR_TIMEOUT.  Later launches are unaffected. */
+int mib_test_inject_wait_expiry(int64_t wait_limit_cycles);
 
 /* Message of the last error returned on this thread. */
 const char* mib_last_error(void);

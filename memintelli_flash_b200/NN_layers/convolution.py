@@ -82,7 +82,11 @@ class Conv2dMem(nn.Module):
         x_sliced = SlicedData(self.input_slice_method, device=input.device, bw_e=self.weight_sliced.bw_e,
                               is_weight=False, paral_size=self.input_paral_size, quant_gran=self.input_quant_gran,
                               inference=inference)
-        x_sliced._slice_conv_imp(self.engine, input.detach(), (kh, kw), (sh, sw), (ph, pw), (dh, dw))
+        # the input is sliced for exactly one multiply: with voltage noise on, the slicing applies that
+        # multiply's noise (drawn with the seed the multiply would draw) and the separate pass is skipped
+        noise_seed = int(torch.randint(0, 2 ** 62, (1,)).item()) if self.engine.conv_input_noise_fused() else None
+        x_sliced._slice_conv_imp(self.engine, input.detach(), (kh, kw), (sh, sw), (ph, pw), (dh, dw),
+                                 noise_seed=noise_seed)
         L = h_out * w_out
         cout = self.out_channels
         out = torch.empty((n, cout, h_out, w_out), dtype=torch.float32, device=self.engine.device)

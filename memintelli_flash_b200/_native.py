@@ -60,6 +60,9 @@ _SIGS = {
                               c_vp, c_vp, c_vp],
     "mib_slice_conv_input": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
                              _P(SliceSpec), _P(KGeom), c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
+    "mib_slice_conv_input_noisy": [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32, c_i32,
+                                   c_i32, _P(SliceSpec), _P(KGeom), c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_f64, c_u64,
+                                   c_u64, c_vp],
     "mib_program_weight": [c_vp, c_i64, c_i64, c_i64, c_i64, _P(SliceSpec), _P(KGeom), _P(DeviceSpec), c_vp, c_vp,
                            c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     "mib_input_noise": [c_vp, c_vp, c_i64, c_f64, c_u64, c_u64, c_vp],
@@ -71,6 +74,7 @@ _SIGS = {
     "mib_mvm_static_scratch": [c_vp, c_vp, c_i64, _P(SliceSpec), c_vp, c_vp, c_i64, _P(SliceSpec), _P(KGeom),
                                _P(DeviceSpec), c_i32, c_vp, c_i32, c_vp, _P(OutLayout), c_vp, c_vp],
     "mib_device_status": [],
+    "mib_test_inject_wait_expiry": [c_i64],
 }
 EXPORTS = tuple(_SIGS) + ("mib_last_error", "mib_version", "mib_launch_count")
 

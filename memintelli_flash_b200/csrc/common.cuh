@@ -53,15 +53,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar`.  Gives up when `abort` is raised by another
-// thread or after kWaitTimeoutCycles; on timeout it raises `abort` and records
+// thread or after `limit` cycles; on timeout it raises `abort` and records
 // `code` in the device error flag.  Returns false when the wait did not complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code,
+                                          long long limit = kWaitTimeoutCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitTimeoutCycles) {
+    if (clock64() - t0 > limit) {
       *abort = 1;
       atomicExch(&g_device_error, code);
       return false;

@@ -24,6 +24,8 @@ struct SliceArgs {
   float* block_max;               // [batch][nbr][nbc]
   float* block_exp;               // same or null
   uint8_t* packed;                // [batch*rows][kp] or null
+  float vnoise;                   // FP16 planes only: per-call voltage noise applied while storing (0: none)
+  uint64_t noise_seed, noise_stream;
 };
 
 struct ProgramArgs {
@@ -48,6 +50,7 @@ struct ProgramArgs {
 
 struct ReadNoiseArgs {
   float qg_f, lgs_f;
+  float inv_qg, lgs_over_qg;      // 1 / Q_G and LGS / Q_G
   int32_t any_sigma, per_level, g_level;
   float sigma[256];
 };
@@ -88,6 +91,8 @@ struct MvmArgs {
   int32_t* acc_dump;        // [Kt][M][N] or null
   int32_t tiles_per_split;  // K tiles per CTA along grid z (== Kt without split-K)
   float* partial;           // split-K: [splits][M][N] fp32 partial outputs, or null
+  int64_t wait_limit;       // cycles after which an abortable mbarrier wait gives up (about 2 s normally)
+  int32_t hold_mma;         // test hook: the MMA warp issues nothing, so the epilogue's first wait runs out
 };
 
 cudaError_t slice_dense(const float* x, int64_t ld_batch, int64_t ld_row, SliceArgs a, cudaStream_t stream);

@@ -22,6 +22,10 @@ namespace {
 
 thread_local std::string g_err;
 
+// One-shot failure injection for tests (mib_test_inject_wait_expiry): the next mib_mvm launch on this
+// thread holds its MMA warp and gives its abortable waits this many cycles.
+thread_local long long g_inject_wait_limit = 0;
+
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
@@ -108,6 +112,8 @@ void fill_slice_args(mib::SliceArgs& a, const SliceTab& t, const mib_slice_spec*
   a.block_max = block_max;
   a.block_exp = block_exp;
   a.packed = packed;
+  a.vnoise = 0.0f;
+  a.noise_seed = a.noise_stream = 0;
 }
 
 int check_input_geom(const SliceTab& t, const mib_slice_spec* sp, const mib_k_geom* kg, int64_t cols, int32_t rdac,
@@ -337,6 +343,13 @@ const char* mib_version(void) { return "memintelli_b200 0.1.0 (sm_100a)"; }
 
 uint64_t mib_launch_count(void) { return mib::launch_count(); }
 
+int mib_test_inject_wait_expiry(int64_t wait_limit_cycles) {
+  if (wait_limit_cycles < 1 || wait_limit_cycles > mib::kWaitTimeoutCycles)
+    return fail(MIB_ERR_PARAM, "wait limit must be in [1, 4e9] cycles");
+  g_inject_wait_limit = wait_limit_cycles;
+  return MIB_OK;
+}
+
 int mib_device_status(void) {
   int v = 0;
   cudaError_t e = cudaDeviceSynchronize();
@@ -432,11 +445,11 @@ int mib_qk_norm_rope_bf16(const float* qkv, int64_t tokens, int64_t ld_token, in
   return MIB_OK;
 }
 
-int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
-                         int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
-                         const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
-                         void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
-                         cudaStream_t stream) {
+static int slice_conv_impl(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
+                           int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
+                           const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                           void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                           double vnoise, uint64_t seed, uint64_t call, cudaStream_t stream) {
   SliceTab t;
   if (int r = make_tab(spec, t)) return r;
   if (!x) return fail(MIB_ERR_PARAM, "input is NULL");
@@ -451,9 +464,35 @@ int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_
   mib::SliceArgs a;
   fill_slice_args(a, t, spec, kg, n, ho * wo, cols, rdac, operand_kind, planes, tile_scale, block_max, block_exp,
                   packed);
+  if (vnoise != 0.0) {
+    if (operand_kind != MIB_OPERAND_FP16) return fail(MIB_ERR_PARAM, "voltage noise needs FP16 planes");
+    if (!(vnoise > 0.0)) return fail(MIB_ERR_PARAM, "voltage noise must be positive");
+    a.vnoise = static_cast<float>(vnoise);
+    a.noise_seed = seed;
+    a.noise_stream = (call << 2) | 1u;   // the stream mib_input_noise draws for this call
+  }
   cudaError_t e = mib::slice_conv(x, c, h, w, ho, wo, kh, kw, sh, sw, ph, pw, dh, dw, a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "slice_conv_input launch");
   return MIB_OK;
+}
+
+int mib_slice_conv_input(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
+                         int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
+                         const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, int32_t operand_kind,
+                         void* planes, float* tile_scale, float* block_max, float* block_exp, uint8_t* packed,
+                         cudaStream_t stream) {
+  return slice_conv_impl(x, n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg, rdac, operand_kind, planes,
+                         tile_scale, block_max, block_exp, packed, 0.0, 0, 0, stream);
+}
+
+int mib_slice_conv_input_noisy(const float* x, int64_t n, int64_t c, int64_t h, int64_t w, int32_t kh, int32_t kw,
+                               int32_t sh, int32_t sw, int32_t ph, int32_t pw, int32_t dh, int32_t dw,
+                               const mib_slice_spec* spec, const mib_k_geom* kg, int32_t rdac, void* planes_fp16,
+                               float* tile_scale, float* block_max, float* block_exp, uint8_t* packed, double vnoise,
+                               uint64_t seed, uint64_t call, cudaStream_t stream) {
+  if (vnoise == 0.0) return fail(MIB_ERR_PARAM, "voltage noise must be positive");
+  return slice_conv_impl(x, n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg, rdac, MIB_OPERAND_FP16, planes_fp16,
+                         tile_scale, block_max, block_exp, packed, vnoise, seed, call, stream);
 }
 
 int mib_program_weight(const float* w, int64_t k, int64_t n, int64_t stride_k, int64_t stride_n,
@@ -543,8 +582,12 @@ int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __h
   if (n_elems % 4) return fail(MIB_ERR_SHAPE, "element count must be a multiple of 4");
   mib::ReadNoiseArgs a;
   memset(&a, 0, sizeof(a));
-  a.qg_f = static_cast<float>((dev->hgs - dev->lgs) / (dev->g_level - 1));
+  if (dev->g_level < 2 || !(dev->lgs < dev->hgs)) return fail(MIB_ERR_PARAM, "invalid conductance levels");
+  const double qg = (dev->hgs - dev->lgs) / (dev->g_level - 1);
+  a.qg_f = static_cast<float>(qg);
   a.lgs_f = static_cast<float>(dev->lgs);
+  a.inv_qg = static_cast<float>(1.0 / qg);
+  a.lgs_over_qg = static_cast<float>(dev->lgs / qg);
   a.g_level = dev->g_level;
   const int ns = std::max(1, dev->n_read_sigma);
   if (ns != 1 && ns != dev->g_level) return fail(MIB_ERR_PARAM, "read variation needs one value or one per level");
@@ -680,6 +723,12 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
     sp = SplitPlan{1, static_cast<int>(kg->kt)};
   a.tiles_per_split = sp.tiles_per_split;
   a.partial = sp.splits > 1 ? workspace : nullptr;
+  a.wait_limit = mib::kWaitTimeoutCycles;
+  if (g_inject_wait_limit > 0) {
+    a.wait_limit = g_inject_wait_limit;
+    a.hold_mma = 1;
+    g_inject_wait_limit = 0;
+  }
   CUtensorMap ta, tb;
   if (int r = encode_planes(&ta, a_planes, operand_kind, m, kg->kt * kg->pp, tx.S, kg->pp, mib::kMvmBM)) return r;
   if (int r = encode_planes(&tb, b_planes, operand_kind, n, kg->kt * kg->pp, tw.S, kg->pp, bn)) return r;

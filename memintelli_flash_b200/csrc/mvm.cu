@@ -43,8 +43,9 @@ struct SmemCtl {
   int abort;
 };
 
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
-  const bool ok = mbar_wait(bar, parity, abort, code);
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int code,
+                                          long long limit) {
+  const bool ok = mbar_wait(bar, parity, abort, code, limit);
   return __all_sync(0xffffffffu, ok);
 }
 
@@ -144,7 +145,7 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       int s = 0;
       uint32_t phase = 0;
       for (int t = 0; t < Kt; ++t) {
-        if (t >= stages && !mbar_wait(&ctl->empty[s], phase ^ 1u, abort, 11)) break;
+        if (t >= stages && !mbar_wait(&ctl->empty[s], phase ^ 1u, abort, 11, P.wait_limit)) break;
         uint8_t* a_dst = smem + static_cast<size_t>(s) * P.stage_bytes;
         uint8_t* b_dst = a_dst + static_cast<size_t>(Sx) * P.a_slice_bytes;
         mbar_arrive_expect_tx(&ctl->full[s], P.stage_bytes);
@@ -168,9 +169,9 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       const int ksteps = P.row_bytes / 32;
       int slot = 0, s = 0, uses = 0;
       uint32_t sphase = 0, tphase = 0;
-      bool ok = true;
+      bool ok = P.hold_mma == 0;   // held (test hook): no MMA and no commit, the epilogue's wait runs out
       for (int t = 0; t < Kt && ok; ++t) {
-        if (!mbar_wait(&ctl->full[s], sphase, abort, 21)) {
+        if (!mbar_wait(&ctl->full[s], sphase, abort, 21, P.wait_limit)) {
           ok = false;
           break;
         }
@@ -178,7 +179,7 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
         const uint32_t a_base = smem_u32(smem + static_cast<size_t>(s) * P.stage_bytes);
         const uint32_t b_base = a_base + Sx * P.a_slice_bytes;
         for (int i = 0; i < Sx; ++i) {
-          if (uses >= kSlots && !mbar_wait(&ctl->tempty[slot], tphase ^ 1u, abort, 22)) {
+          if (uses >= kSlots && !mbar_wait(&ctl->tempty[slot], tphase ^ 1u, abort, 22, P.wait_limit)) {
             ok = false;
             break;
           }
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     for (int t = 0; t < Kt && ok; ++t) {
 #pragma unroll kSxUnroll
       for (int i = 0; i < Sx; ++i) {
-        if (!warp_wait(&ctl->tfull[slot], tphase, abort, 31)) {
+        if (!warp_wait(&ctl->tfull[slot], tphase, abort, 31, P.wait_limit)) {
           ok = false;
           break;
         }

@@ -136,6 +136,28 @@ __device__ __forceinline__ void build_level_lut(LevelLut<KIND>& lut, const Slice
   __syncthreads();
 }
 
+// Voltage noise of one plane element (memmat_tensor.py:297-299): level * (1 + vnoise * z), with explicit
+// roundings so that the fused (slicing) and separate (input_noise_kernel) passes give the same bits.
+__device__ __forceinline__ float apply_vnoise(float v, float z, float vnoise) {
+  return __fmul_rn(v, __fmaf_rn(z, vnoise, 1.0f));
+}
+
+// Voltage noise on 4 FP16 plane elements starting at linear plane index idx (idx % 4 == 0): they are
+// Philox group idx / 4 of the call's input-noise stream, as in input_noise_kernel.
+__device__ __forceinline__ uint2 vnoise4(uint2 o, const SliceArgs& a, int64_t idx) {
+  float z[4];
+  normal4(a.noise_seed, a.noise_stream, static_cast<uint64_t>(idx >> 2), z);
+  const __half2 h0 = *reinterpret_cast<const __half2*>(&o.x), h1 = *reinterpret_cast<const __half2*>(&o.y);
+  const __half2 n0 = __floats2half2_rn(apply_vnoise(__low2float(h0), z[0], a.vnoise),
+                                       apply_vnoise(__high2float(h0), z[1], a.vnoise));
+  const __half2 n1 = __floats2half2_rn(apply_vnoise(__low2float(h1), z[2], a.vnoise),
+                                       apply_vnoise(__high2float(h1), z[3], a.vnoise));
+  uint2 r;
+  r.x = *reinterpret_cast<const uint32_t*>(&n0);
+  r.y = *reinterpret_cast<const uint32_t*>(&n1);
+  return r;
+}
+
 // Write the planes of 4 consecutive positions (codes q0..q3) starting at element offset dst.
 // S > 0 fixes the slice count at compile time; S == 0 reads it from the arguments.
 template <int KIND, int S>
@@ -166,6 +188,7 @@ __device__ __forceinline__ void store_planes4(const LevelLut<KIND>& lut, const S
       uint2 o;
       o.x = __byte_perm(lut.w[q0][wk], lut.w[q1][wk], sel);
       o.y = __byte_perm(lut.w[q2][wk], lut.w[q3][wk], sel);
+      if (a.vnoise != 0.0f) o = vnoise4(o, a, t * a.plane_stride + dst);
       *reinterpret_cast<uint2*>(base + t * a.plane_stride) = o;
     }
   }
@@ -570,8 +593,8 @@ __global__ void input_noise_kernel(const uint8_t* __restrict__ in, __half* __res
       normal4(seed, stream, 2 * static_cast<uint64_t>(i) + 1, z1);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        v[u] = v[u] * (1.0f + z0[u] * vnoise);
-        v[4 + u] = v[4 + u] * (1.0f + z1[u] * vnoise);
+        v[u] = apply_vnoise(v[u], z0[u], vnoise);
+        v[4 + u] = apply_vnoise(v[4 + u], z1[u], vnoise);
       }
     }
     __half2 h[4];
@@ -581,46 +604,79 @@ __global__ void input_noise_kernel(const uint8_t* __restrict__ in, __half* __res
   }
 }
 
-// 4 elements per thread: conductance from levels (or fp32 G planes), read
-// variation G*exp(sigma*N), output (G' - LGS)/Q_G as FP16.
+// Read variation of one group of 4 cells (memmat_tensor.py:204-236): G' = G exp(sigma z) with one standard
+// normal z per cell (Philox group `grp`), output (G' - LGS) / Q_G as FP16.  From an E4M3 level L
+// (G = L Q_G + LGS) the output is L e + (LGS / Q_G)(e - 1) with e = exp(sigma z): no division, and L
+// itself indexes a per-level sigma (the reference recovers it as round((G - LGS) / Q_G)).  Conductance
+// planes (write variation present) go through G directly.
+__device__ __forceinline__ uint2 read_noise_group(uint32_t lv_raw, const float* __restrict__ gp, int64_t grp,
+                                                  const ReadNoiseArgs& a, uint64_t seed, uint64_t stream) {
+  float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (a.any_sigma) normal4(seed, stream, static_cast<uint64_t>(grp), z);
+  float o[4];
+  if (gp) {
+    const float4 g4 = reinterpret_cast<const float4*>(gp)[grp];
+    const float g[4] = {g4.x, g4.y, g4.z, g4.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float gg = g[u];
+      if (a.any_sigma) {
+        float sigma = a.sigma[0];
+        if (a.per_level) {
+          int lv = static_cast<int>(rintf((gg - a.lgs_f) / a.qg_f));
+          sigma = a.sigma[min(max(lv, 0), a.g_level - 1)];
+        }
+        gg = gg * __expf(z[u] * sigma);  // approximate hardware exp: the noise is statistical
+      }
+      o[u] = (gg - a.lgs_f) * a.inv_qg;
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float L = dec_e4m3(static_cast<uint8_t>(lv_raw >> (8 * u)));
+      if (a.any_sigma) {
+        const float sigma = a.per_level ? a.sigma[min(static_cast<int>(L), a.g_level - 1)] : a.sigma[0];
+        const float e = __expf(z[u] * sigma);
+        o[u] = fmaf(L, e, a.lgs_over_qg * (e - 1.0f));
+      } else {
+        o[u] = L;
+      }
+    }
+  }
+  const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
+  uint2 r;
+  r.x = *reinterpret_cast<const uint32_t*>(&h0);
+  r.y = *reinterpret_cast<const uint32_t*>(&h1);
+  return r;
+}
+
+// Two 4-cell groups per thread (8 B of levels in, 16 B of FP16 out) when the buffers allow the wide
+// accesses, else one group per thread.  Group g always draws Philox block g, so both forms give the
+// same values.
+template <bool WIDE>
 __global__ void read_noise_kernel(const uint8_t* __restrict__ levels, const float* __restrict__ gp,
                                   __half* __restrict__ out, int64_t n4, ReadNoiseArgs a, uint64_t seed,
                                   uint64_t stream) {
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    float g[4];
-    if (gp) {
-      const float4 g4 = reinterpret_cast<const float4*>(gp)[i];
-      g[0] = g4.x;
-      g[1] = g4.y;
-      g[2] = g4.z;
-      g[3] = g4.w;
-    } else {
-      const uint32_t raw = reinterpret_cast<const uint32_t*>(levels)[i];
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-        g[u] = __fadd_rn(__fmul_rn(dec_e4m3(static_cast<uint8_t>(raw >> (8 * u))), a.qg_f), a.lgs_f);
+  const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  if constexpr (WIDE) {
+    const int64_t n8 = n4 / 2;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += step) {
+      uint2 raw = make_uint2(0u, 0u);
+      if (!gp) raw = reinterpret_cast<const uint2*>(levels)[i];
+      const uint2 o0 = read_noise_group(raw.x, gp, 2 * i, a, seed, stream);
+      const uint2 o1 = read_noise_group(raw.y, gp, 2 * i + 1, a, seed, stream);
+      reinterpret_cast<uint4*>(out)[i] = make_uint4(o0.x, o0.y, o1.x, o1.y);
     }
-    if (a.any_sigma) {
-      float z[4];
-      normal4(seed, stream, static_cast<uint64_t>(i), z);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        float sigma = a.sigma[0];
-        if (a.per_level) {
-          int lv = static_cast<int>(rintf((g[u] - a.lgs_f) / a.qg_f));
-          lv = min(max(lv, 0), a.g_level - 1);
-          sigma = a.sigma[lv];
-        }
-        g[u] = g[u] * __expf(z[u] * sigma);  // approximate hardware exp: the noise is statistical
-      }
+    if ((n4 & 1) && blockIdx.x == 0 && threadIdx.x == 0) {
+      const int64_t g = n4 - 1;
+      const uint32_t raw = gp ? 0u : reinterpret_cast<const uint32_t*>(levels)[g];
+      reinterpret_cast<uint2*>(out)[g] = read_noise_group(raw, gp, g, a, seed, stream);
     }
-    __half2 h0 = __floats2half2_rn((g[0] - a.lgs_f) / a.qg_f, (g[1] - a.lgs_f) / a.qg_f);
-    __half2 h1 = __floats2half2_rn((g[2] - a.lgs_f) / a.qg_f, (g[3] - a.lgs_f) / a.qg_f);
-    uint2 o;
-    o.x = *reinterpret_cast<uint32_t*>(&h0);
-    o.y = *reinterpret_cast<uint32_t*>(&h1);
-    reinterpret_cast<uint2*>(out)[i] = o;
+  } else {
+    for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < n4; g += step) {
+      const uint32_t raw = gp ? 0u : reinterpret_cast<const uint32_t*>(levels)[g];
+      reinterpret_cast<uint2*>(out)[g] = read_noise_group(raw, gp, g, a, seed, stream);
+    }
   }
 }
 
@@ -793,7 +849,12 @@ cudaError_t input_noise(const uint8_t* in, __half* out, int64_t n, float vnoise,
 cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, int64_t n, ReadNoiseArgs a, uint64_t seed,
                        uint64_t stream_id, cudaStream_t stream) {
   const int64_t n4 = n / 4;
-  read_noise_kernel<<<grid_for(n4, 256), 256, 0, stream>>>(levels, gp, out, n4, a, seed, stream_id);
+  const bool wide = (reinterpret_cast<uintptr_t>(levels) % 8 == 0) && (reinterpret_cast<uintptr_t>(gp) % 32 == 0) &&
+                    (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+  if (wide)
+    read_noise_kernel<true><<<grid_for(n4 / 2 + 1, 256), 256, 0, stream>>>(levels, gp, out, n4, a, seed, stream_id);
+  else
+    read_noise_kernel<false><<<grid_for(n4, 256), 256, 0, stream>>>(levels, gp, out, n4, a, seed, stream_id);
   count_launch();
   return cudaGetLastError();
 }

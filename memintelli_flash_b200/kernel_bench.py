@@ -2,6 +2,7 @@
 
     python -m memintelli_flash_b200.kernel_bench slice --rows 16384 --cols 3072 [--bfp]
     python -m memintelli_flash_b200.kernel_bench mvm --m 4096 --k 4096 --n 4096 [--noisy]
+    python -m memintelli_flash_b200.kernel_bench noise --k 1024 --n 151936 [--per-level]
     python -m memintelli_flash_b200.kernel_bench workload [--config 0 1 2 3]
 
 The engine is the reference's example device (HGS 1e-5, LGS 1e-8, rdac 4, g_level 4,
@@ -88,6 +89,46 @@ def bench_mvm(m, k, n, noisy=False, bfp=False, iters=10, device="cuda:0"):
     print(f"mvm m={m} k={k} n={n} noisy={noisy} bfp={bfp}: {ms:.3f} ms, {ops / ms / 1e9:.1f} slice-pair TOPS, "
           f"{adc / ms / 1e9:.3f} T ADC events/s", flush=True)
     return ms
+
+
+def bench_noise(k, n, iters=20, per_level=False, device="cuda:0"):
+    """Per-call noise passes over the planes of a programmed k x n weight (5 slices, E4M3 levels) and of a
+    k-wide input of n rows: read variation (1 B level in, 2 B FP16 out per cell) and voltage noise (1 B in,
+    2 B out per element).  Prints time per call and algorithmic GB/s."""
+    dev = torch.device(device)
+    sigma = {0: 0.02, 1: 0.05, 2: 0.05, 3: 0.1} if per_level else 0.05
+    eng = DPETensor(HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0,
+                    read_variation=sigma, vnoise=0.05, rdac=4, g_level=4, radc=4096, device=dev)
+    ws = _weight(dev, False)
+    ws.slice_data_imp(eng, torch.randn(k, n, device=dev))
+    planes = ws._buf["planes"]
+    out = torch.empty(planes.shape, dtype=torch.float16, device=dev)
+    spec = eng._device_spec()
+    stream = N.stream_ptr(dev)
+    res = {}
+
+    def run(name, fn, nbytes):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1e3 / iters
+        res[name] = (us, nbytes / us / 1e3)
+        print(f"{name} {planes.numel() / 1e6:.1f} M cells: {us:.1f} us/call, {nbytes / us / 1e3:.0f} GB/s algorithmic",
+              flush=True)
+
+    run("read_noise" + ("_per_level" if per_level else ""), lambda: N.call(
+        "mib_weight_read_noise", N.ptr(planes), None, N.ptr(out), planes.numel(), spec, 7, 1, stream),
+        3 * planes.numel())
+    run("input_noise", lambda: N.call("mib_input_noise", N.ptr(planes), N.ptr(out), planes.numel(), 0.05, 7, 1,
+                                      stream), 3 * planes.numel())
+    N.device_status()
+    return res
 
 
 # ----------------------------------------------------------------------------- layer workloads
@@ -250,6 +291,11 @@ def main(argv=None):
     v.add_argument("--noisy", action="store_true")
     v.add_argument("--bfp", action="store_true")
     v.add_argument("--iters", type=int, default=10)
+    z = sub.add_parser("noise")
+    z.add_argument("--k", type=int, default=1024)
+    z.add_argument("--n", type=int, default=151936)
+    z.add_argument("--per-level", action="store_true")
+    z.add_argument("--iters", type=int, default=20)
     w = sub.add_parser("workload")
     w.add_argument("--config", type=int, nargs="+", default=[0, 1, 2, 3])
     w.add_argument("--iters", type=int, default=5)
@@ -258,6 +304,8 @@ def main(argv=None):
         bench_slice(a.rows, a.cols, a.bfp, a.iters)
     elif a.kernel == "mvm":
         bench_mvm(a.m, a.k, a.n, a.noisy, a.bfp, a.iters)
+    elif a.kernel == "noise":
+        bench_noise(a.k, a.n, a.iters, a.per_level)
     else:
         for c in a.config:
             bench_workload(c, a.iters)

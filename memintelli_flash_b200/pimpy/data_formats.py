@@ -190,8 +190,9 @@ class SlicedData(object):
                 engine._slice_input(self, data)
         self.shape = data.shape
 
-    def _slice_conv_imp(self, engine, x, kernel_size, stride, padding, dilation):
-        """Slice the unfolded view of an NCHW input without materialising it (Conv2dMem)."""
+    def _slice_conv_imp(self, engine, x, kernel_size, stride, padding, dilation, noise_seed=None):
+        """Slice the unfolded view of an NCHW input without materialising it (Conv2dMem).  With
+        ``noise_seed`` the planes already carry the voltage noise of the one multiply made with them."""
         x = x.to(engine.device).detach()
         if x.device.type != "cuda":
             raise RuntimeError("memintelli_flash_b200 computes on CUDA devices only")
@@ -200,7 +201,7 @@ class SlicedData(object):
         self._cache = {}
         self._overrides = {}
         with N.device_guard(x.device):
-            engine._slice_conv_input(self, x, kernel_size, stride, padding, dilation)
+            engine._slice_conv_input(self, x, kernel_size, stride, padding, dilation, noise_seed=noise_seed)
 
     # ------------------------------------------------- reference-layout views
     def _get(self, name, fn):

@@ -227,7 +227,17 @@ class DPETensor(object):
             "mib_slice_swiglu_input", N.ptr(x3), B, T, width, x3.stride(0), x3.stride(1), width, spec, kg,
             int(self.rdac), pkind, *bufs, N.stream_ptr(x3.device)), fallback, tuple(gate_up.shape[:-1]) + (width,))
 
-    def _slice_conv_input(self, sd: SlicedData, x: torch.Tensor, kernel_size, stride, padding, dilation):
+    def conv_input_noise_fused(self) -> bool:
+        """Whether a convolution input sliced once per multiply (Conv2dMem) gets this call's voltage noise
+        inside the slicing: E4M3-sized levels with voltage noise on.  The multiply then skips its
+        separate noise pass; the values are the same."""
+        return self.vnoise > 0 and self.operand_kind == N.OPERAND_E4M3
+
+    def _slice_conv_input(self, sd: SlicedData, x: torch.Tensor, kernel_size, stride, padding, dilation,
+                          noise_seed=None):
+        """Slice the unfolded view of an NCHW input.  With ``noise_seed`` the planes are FP16 with the voltage
+        noise of the multiply drawn with that seed already applied (mib_slice_conv_input_noisy); that
+        multiply must be the next and only one made with ``sd``."""
         x = x.contiguous()
         n, c, h, w = x.shape
         kh, kw = kernel_size
@@ -239,11 +249,18 @@ class DPETensor(object):
         T, K = ho * wo, c * kh * kw
         qg = _decode_gran(sd.quant_gran, sd.paral_size, T, K)
         kind = self.operand_kind
-        pkind = self._input_plane_kind(kind)
         geom = self._k_geom(K, qg[1], int(sd.paral_size[1]), kind)
-        self._run_input_slicing(sd, kind, geom, qg, n, T, K, False, lambda spec, kg, bufs: N.call(
-            "mib_slice_conv_input", N.ptr(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg,
-            int(self.rdac), pkind, *bufs, N.stream_ptr(x.device)), pkind)
+        if noise_seed is not None:
+            self._run_input_slicing(sd, kind, geom, qg, n, T, K, False, lambda spec, kg, bufs: N.call(
+                "mib_slice_conv_input_noisy", N.ptr(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg,
+                int(self.rdac), *bufs, float(self.vnoise), int(noise_seed), 0, N.stream_ptr(x.device)),
+                N.OPERAND_FP16)
+            sd._buf.update(noise_seed=int(noise_seed), vnoise=float(self.vnoise))
+        else:
+            pkind = self._input_plane_kind(kind)
+            self._run_input_slicing(sd, kind, geom, qg, n, T, K, False, lambda spec, kg, bufs: N.call(
+                "mib_slice_conv_input", N.ptr(x), n, c, h, w, kh, kw, sh, sw, ph, pw, dh, dw, spec, kg,
+                int(self.rdac), pkind, *bufs, N.stream_ptr(x.device)), pkind)
         sd.shape = torch.Size((n, T, K))
 
     def _run_input_slicing(self, sd, kind, geom, qg, B, T, K, squeeze, launch, plane_kind=None):
@@ -370,8 +387,18 @@ class DPETensor(object):
         if self.noisy:
             if kind != N.OPERAND_E4M3:
                 raise NotImplementedError('noisy crossbars with more than 16 DAC / conductance levels')
-            seed = int(torch.randint(0, 2 ** 62, (1,)).item())
-            if a_planes.dtype == torch.float16:
+            fused_seed = x._buf.get("noise_seed")
+            if fused_seed is not None:
+                # sliced with this multiply's voltage noise already applied (conv input, sliced per multiply)
+                if x._buf.get("noise_used") or x._buf.get("vnoise") != float(self.vnoise):
+                    raise ValueError('this sliced input carries the voltage noise of one multiply; slice it again')
+                x._buf["noise_used"] = True
+                seed = fused_seed
+            else:
+                seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+            if fused_seed is not None:
+                a16 = a_planes
+            elif a_planes.dtype == torch.float16:
                 # sliced straight to FP16 for an engine without voltage noise (_input_plane_kind)
                 if self.vnoise != 0:
                     raise ValueError('the input was sliced for vnoise=0; slice it again after changing vnoise')

@@ -95,3 +95,43 @@ def test_linear_errors(cuda):
     layer.inference_mode = True
     with pytest.raises(ValueError):
         layer(torch.randn(4, 65, device=cuda))
+
+
+@pytest.mark.parametrize("bfp", [None, 8])
+def test_conv_voltage_noise_fused_into_slicing_equals_separate_pass(bfp, cuda):
+    """Conv2dMem with voltage noise slices its input once per multiply and applies that multiply's voltage
+    noise while writing the FP16 planes (mib_slice_conv_input_noisy).  Under the same torch seed this equals,
+    bit for bit, slicing to E4M3 and running the separate noise pass inside the multiply."""
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200.NN_layers import Conv2dMem
+    eng = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=1024, write_variation=0.0,
+                      rate_stuck_HGS=0.0, rate_stuck_LGS=0.0, read_variation=0.05, vnoise=0.05)
+    assert eng.conv_input_noise_fused()
+    torch.manual_seed(3)
+    layer = Conv2dMem(eng, 16, 32, 3, [1, 1, 2, 2, 2], [1, 1, 2, 2, 2], stride=1, padding=1, bias=True,
+                      device=cuda, bw_e=bfp, input_paral_size=(1, 32), weight_paral_size=(32, 32),
+                      input_quant_gran=(1, 64), weight_quant_gran=(64, 64))
+    layer.inference_mode = True
+    x = torch.randn(4, 16, 12, 12, device=cuda)
+    torch.manual_seed(11)
+    y_fused = layer(x)
+    # the separate path: E4M3 slicing, then the multiply draws the seed and runs the noise pass
+    torch.manual_seed(11)
+    xs = M.SlicedData(layer.input_slice_method, device=cuda, bw_e=bfp, is_weight=False, paral_size=(1, 32),
+                      quant_gran=(1, 64), inference=True)
+    xs._slice_conv_imp(eng, x, (3, 3), (1, 1), (1, 1), (1, 1))
+    assert xs._buf["planes"].dtype == torch.uint8
+    from memintelli_flash_b200 import _native as N
+    out = torch.empty_like(y_fused)
+    L = 12 * 12
+    eng.MapReduceDot(xs, layer.weight_sliced, out=out, bias=layer.bias.detach().float(),
+                     layout=N.OutLayout(L, 32 * L, 1, L))
+    torch.cuda.synchronize()
+    assert torch.equal(y_fused, out)
+    # a second multiply with a fused-noise input would reuse its draw: rejected
+    xs2 = M.SlicedData(layer.input_slice_method, device=cuda, bw_e=bfp, is_weight=False, paral_size=(1, 32),
+                       quant_gran=(1, 64), inference=True)
+    xs2._slice_conv_imp(eng, x, (3, 3), (1, 1), (1, 1), (1, 1), noise_seed=5)
+    eng.MapReduceDot(xs2, layer.weight_sliced, out=out, layout=N.OutLayout(L, 32 * L, 1, L))
+    with pytest.raises(ValueError, match="one multiply"):
+        eng.MapReduceDot(xs2, layer.weight_sliced, out=out, layout=N.OutLayout(L, 32 * L, 1, L))

@@ -176,3 +176,66 @@ def test_small_model_bf16_attention_close_to_reference(cuda):
     print(f"bf16 attention vs reference model {d:.2e}")
     assert d <= 2e-2
     assert abs(float(model(ids)) - float(fx["loss_r289"][0])) <= 5e-3
+
+
+def _swap_linears(module, mem_args):
+    """Every nn.Linear replaced by this library's LinearMem with the keyword arguments the reference's
+    Qwen3 wrapper passes (memintelli/NN_models/Qwen3.py:82-106), weights copied over."""
+    from memintelli_flash_b200.NN_layers import LinearMem
+    for name, child in list(module.named_children()):
+        if isinstance(child, torch.nn.Linear):
+            new = LinearMem(engine=mem_args["engine"], in_features=child.in_features,
+                            out_features=child.out_features, input_slice=mem_args["input_slice"],
+                            weight_slice=mem_args["weight_slice"], bias=child.bias is not None,
+                            device=mem_args["device"], bw_e=mem_args["bw_e"],
+                            input_paral_size=mem_args["input_paral_size"],
+                            weight_paral_size=mem_args["weight_paral_size"],
+                            input_quant_gran=mem_args["input_quant_gran"],
+                            weight_quant_gran=mem_args["weight_quant_gran"])
+            with torch.no_grad():
+                new.weight.copy_(child.weight.data)
+                if child.bias is not None:
+                    new.bias.copy_(child.bias.data)
+            setattr(module, name, new)
+        else:
+            _swap_linears(child, mem_args)
+
+
+def test_hf_qwen3_with_linearmem_swapped_in_matches_reference(cuda):
+    """Drop-in at the layer level: transformers' Qwen3ForCausalLM with its nn.Linear layers swapped for this
+    library's LinearMem, programmed with update_weight() and switched to inference as the reference's
+    Qwen3MemWrapper does, against the reference-built model's logits (tie-free radc 289, fp32 eager
+    attention on both sides)."""
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden"))
+    import qwen3_small as Q
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200.NN_layers import LinearMem
+    from transformers import Qwen3ForCausalLM
+    fx = dict(np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "qwen3_model.npz")))
+    torch.manual_seed(0)
+    model = Qwen3ForCausalLM(Q.hf_config())
+    model.load_state_dict(Q.state_dict())
+    model.to(cuda)
+    eng = M.DPETensor(device=cuda, **dict(NOISE_FREE, radc=289))
+    _swap_linears(model, dict(engine=eng, input_slice=[1, 1, 2, 2, 2], weight_slice=[1, 1, 2, 2, 2], device=cuda,
+                              bw_e=None, input_paral_size=(1, 32), weight_paral_size=(32, 32),
+                              input_quant_gran=(1, 128), weight_quant_gran=(128, 128)))
+    n_mem = 0
+    for m in model.modules():
+        if isinstance(m, LinearMem):
+            m.update_weight()
+            m.inference_mode = True
+            m.weight_sliced.inference = True
+            n_mem += 1
+    assert n_mem == 2 * 7 + 1
+    model.eval()
+    ids = torch.from_numpy(fx["ids"]).to(cuda)
+    with torch.no_grad():
+        res = model(input_ids=ids, labels=ids)
+    logits = res.logits.double().cpu().numpy()
+    ref = fx["logits_r289"].astype(np.float64)
+    d = _rel(logits, ref)
+    print(f"HF Qwen3 + LinearMem vs reference model: {d:.2e}")
+    assert d <= 5e-3
+    assert abs(float(res.loss) - float(fx["loss_r289"][0])) <= 1e-3

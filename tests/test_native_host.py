@@ -183,3 +183,16 @@ def test_static_scratch_rejects_oversized_split_before_any_launch():
     assert L.mib_mvm_static_scratch(fake, fake, 128, xs, fake, fake, 4800, ws, kg, dev, 0, None, 0, fake, lay,
                                     None, None) == N.MIB_ERR_UNSUPPORTED
     assert b"built-in scratch" in L.mib_last_error()
+
+
+def test_noisy_conv_slicing_and_failure_injection_check_arguments():
+    L = N.lib()
+    fake = ctypes.c_void_p(0x1000)
+    xs = _spec(SM, (1, 32), (1, 64))
+    kg = _kg(144, qg=64)                     # 16 channels x 3 x 3 = 144 columns, padded to 192
+    args = (fake, 2, 16, 8, 8, 3, 3, 1, 1, 1, 1, 1, 1, xs, kg, 4, fake, fake, fake, None, None)
+    assert L.mib_slice_conv_input_noisy(*args, 0.0, 1, 0, None) == N.MIB_ERR_PARAM   # no noise: use the plain entry
+    assert L.mib_slice_conv_input_noisy(*args, -0.1, 1, 0, None) == N.MIB_ERR_PARAM
+    assert L.mib_slice_conv_input_noisy(None, *args[1:], 0.05, 1, 0, None) == N.MIB_ERR_PARAM
+    assert L.mib_test_inject_wait_expiry(0) == N.MIB_ERR_PARAM
+    assert L.mib_test_inject_wait_expiry(5_000_000_000) == N.MIB_ERR_PARAM
