@@ -189,6 +189,20 @@ bool noise_free(const mib_device_spec* d) {
   return true;
 }
 
+// Largest factor by which per-call noise can raise a crossbar sum above its noise-free full scale.  The
+// normals come from Box-Muller on 24-bit uniforms in (0, 1] (common.cuh normal4), so |z| <= sqrt(-2 ln 2^-24)
+// = 5.77: read variation scales a cell by at most exp(5.8 sigma) (plus (LGS/Q_G)(e - 1) < 0.01 of a level
+// here), voltage noise an input level by at most 1 + 5.8 vnoise.  Write variation is a torch.normal field
+// without that bound, so it keeps a factor of 2.
+double noisy_sum_factor(const mib_device_spec* d) {
+  double smax = 0.0;
+  for (int i = 0; i < std::max(1, d->n_read_sigma); ++i) smax = std::max(smax, static_cast<double>(d->read_sigma[i]));
+  double f = std::exp(5.8 * smax) * 1.01;
+  if (d->vnoise > 0.0) f *= 1.0 + 5.8 * d->vnoise;
+  if (d->write_variation > 0.0) f *= 2.0;
+  return f;
+}
+
 struct AdcPlan {
   int mode = 0;          // MODE_LUT / MODE_FLOATACC bits
   int lut_len = 0;       // entries per weight slice
@@ -266,7 +280,7 @@ int adc_plan(const SliceTab& tx, const SliceTab& tw, const mib_slice_spec* xs, c
     for (int j = 0; j < tw.S; ++j) wsum += std::llabs(tx.maxes[i] * tw.maxes[j] * tx.coef[i] * tw.coef[j]);
   long long qmax = 0;
   for (int j = 0; j < tw.S; ++j) qmax = std::max(qmax, pl.R[j]);
-  if (!exact) qmax *= 2;  // noisy crossbar sums can exceed the nominal full scale
+  if (!exact) qmax = static_cast<long long>(std::ceil(static_cast<double>(qmax) * noisy_sum_factor(dev))) + 2;
   const double limit = 0.98 * 2147483648.0;
   const double per_tile = static_cast<double>(wsum) * static_cast<double>(qmax);
   if (!uniform || per_tile >= limit) {
