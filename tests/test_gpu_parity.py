@@ -189,3 +189,24 @@ def test_conv_patch_slicing(k, s, p, d, bfp, gran, cuda):
                          paral_size=(1, 32), quant_gran=gran)
     assert np.array_equal(sd._buf["block_max"].cpu().numpy().reshape(ref.bmax.shape), ref.bmax)
     assert np.array_equal(sd.sliced_data.cpu().numpy(), ref.sliced_data())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_engine_on_second_device_while_first_is_current():
+    """The MVM raises its shared-memory attribute per device, and the host layer switches to the operands'
+    device around every native call: an engine on cuda:1 works while cuda:0 is current, and matches the
+    oracle (a first launch on cuda:0 sets the attribute there only)."""
+    c = G.case("cfg0_int")
+    dev0, dev1 = torch.device("cuda:0"), torch.device("cuda:1")
+    torch.cuda.set_device(dev0)
+    eng0, xs0, ws0 = gpu_pair(c, dev0)
+    y0 = eng0(xs0, ws0)
+    eng1, xs1, ws1 = gpu_pair(c, dev1)
+    assert torch.cuda.current_device() == 0
+    y1 = eng1(xs1, ws1)
+    assert y1.device == dev1 and torch.cuda.current_device() == 0
+    torch.cuda.synchronize(dev1)
+    oxs, ows, oeng, wl = oracle_pair(c)
+    ref = O.mvm_exact(oxs, ows, oeng, wl)
+    assert rel_norm(y1.double().cpu().numpy(), ref) <= 1e-5
+    assert torch.equal(y0.cpu(), y1.cpu())
