@@ -375,7 +375,10 @@ def run_b200(args):
             grp = dist.new_group(ranks)
             if rank // tp == r:
                 tp_group = grp
-    torch.manual_seed(1234 + rank)
+    # one seed on every rank: each forward draws the same per-call read noise everywhere, so data-parallel
+    # ranks compute rows of the single-GPU forward (one draw per linear shared by all sequences, as in one
+    # reference call) instead of independent replicas
+    torch.manual_seed(1234)
     engine = DPETensor(device=dev, **ENGINE)
     model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=tp_group)
     torch.cuda.synchronize()

@@ -239,6 +239,16 @@ int mib_qk_norm_rope_bf16(const float* qkv, int64_t tokens, int64_t ld_token, in
                           const float* cos_table, const float* sin_table, void* q_out, void* k_out, void* v_out,
                           cudaStream_t stream);
 
+/* Row log-sum-exp of a logit block for the Qwen3 prefill driver's loss (outside the reference's CIM path, no
+ * reference counterpart; the reference's HF model computes the loss in torch).  For each row r of the
+ * (rows, cols) block at logits[r * ld + c]: row_max[r] = max_c, row_sumexp[r] = sum_c exp(logit - row_max[r]),
+ * and, when target_logit is non-NULL, target_logit[r] = the logit at column targets[r] - target_offset if
+ * that column is inside the block, else 0.  Vocabulary shards combine as M = max over shards,
+ * S = sum of row_sumexp * exp(row_max - M), loss = log S + M - target. */
+int mib_row_logsumexp(const float* logits, int64_t rows, int64_t cols, int64_t ld, const int64_t* targets,
+                      int64_t target_offset, float* row_max, float* row_sumexp, float* target_logit,
+                      cudaStream_t stream);
+
 /* Reads and clears the device-side error flag of the current device (synchronises it).
  * Returns MIB_OK, or MIB_ERR_TIMEOUT when a kernel gave up a bounded wait. */
 int mib_device_status(void);

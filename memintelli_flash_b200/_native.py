@@ -73,6 +73,7 @@ _SIGS = {
     "mib_mvm_workspace": [c_i64, c_i64, _P(SliceSpec), _P(SliceSpec), _P(KGeom), _P(DeviceSpec), _P(c_i64)],
     "mib_mvm_static_scratch": [c_vp, c_vp, c_i64, _P(SliceSpec), c_vp, c_vp, c_i64, _P(SliceSpec), _P(KGeom),
                                _P(DeviceSpec), c_i32, c_vp, c_i32, c_vp, _P(OutLayout), c_vp, c_vp],
+    "mib_row_logsumexp": [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp],
     "mib_device_status": [],
     "mib_test_inject_wait_expiry": [c_i64],
 }

@@ -111,6 +111,9 @@ void launch_block_exp(const float* bmax, float* bexp, int64_t n, cudaStream_t st
 cudaError_t qk_norm_rope(const float* qkv, int64_t tokens, int64_t ld_token, int seq_len, int q_heads, int kv_heads,
                          int head_dim, const float* q_norm, const float* k_norm, float eps, const float* cos_t,
                          const float* sin_t, void* q_out, void* k_out, void* v_out, cudaStream_t stream);
+cudaError_t row_lse(const float* x, int64_t rows, int64_t cols, int64_t ld, const int64_t* targets,
+                    int64_t target_offset, float* row_max, float* row_sumexp, float* target_logit,
+                    cudaStream_t stream);
 void count_launch(int n = 1);
 size_t mvm_smem_bytes(const MvmArgs& a);
 cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, int64_t N, float* y,

@@ -17,6 +17,7 @@
 #include "slice.cu"
 #include "mvm.cu"
 #include "attn_prep.cu"
+#include "row_lse.cu"
 
 namespace {
 
@@ -487,6 +488,17 @@ static int slice_conv_impl(const float* x, int64_t n, int64_t c, int64_t h, int6
   }
   cudaError_t e = mib::slice_conv(x, c, h, w, ho, wo, kh, kw, sh, sw, ph, pw, dh, dw, a, stream);
   if (e != cudaSuccess) return cuda_fail(e, "slice_conv_input launch");
+  return MIB_OK;
+}
+
+int mib_row_logsumexp(const float* logits, int64_t rows, int64_t cols, int64_t ld, const int64_t* targets,
+                      int64_t target_offset, float* row_max, float* row_sumexp, float* target_logit,
+                      cudaStream_t stream) {
+  if (!logits || !row_max || !row_sumexp || (target_logit && !targets)) return fail(MIB_ERR_PARAM, "NULL buffer");
+  if (rows < 1 || cols < 1 || ld < cols) return fail(MIB_ERR_SHAPE, "invalid logit block");
+  cudaError_t e = mib::row_lse(logits, rows, cols, ld, targets, target_offset, row_max, row_sumexp, target_logit,
+                               stream);
+  if (e != cudaSuccess) return cuda_fail(e, "row_logsumexp launch");
   return MIB_OK;
 }
 

@@ -12,9 +12,12 @@ compactly so that its crossbars can be sharded across GPUs:
 * lm_head is column-sharded and the cross-entropy is computed without
   gathering the logits (distributed log-sum-exp).
 
-With a world size of 1 there is no collective and no sharding.  The
-non-CIM parts (embedding, RMSNorm, RoPE, attention, SiLU, loss) run in torch;
-attention runs in bf16 through scaled_dot_product_attention.
+With a world size of 1 there is no collective and no sharding.  Of the
+non-CIM parts, the RMSNorms and the SwiGLU run inside the input slicing, q/k
+RMSNorm + RoPE in one kernel (mib_qk_norm_rope_bf16), the loss's row
+log-sum-exp in one pass over the logits (mib_row_logsumexp); the embedding
+and the residual adds stay in torch, and attention runs in bf16 through
+scaled_dot_product_attention (or fp32, ``set_attention_dtype``).
 """
 from __future__ import annotations
 
@@ -295,16 +298,24 @@ class Qwen3CimPrefill(torch.nn.Module):
         return torch.cat(hs, dim=0)
 
     def _sharded_ce(self, logits, target):
-        """Mean cross-entropy over column-sharded logits (no gather of the vocabulary)."""
-        lo, hi = self.lm_head.lo, self.lm_head.hi
-        lmax = logits.max(dim=-1).values
+        """Mean cross-entropy over column-sharded logits (no gather of the vocabulary).  One pass over this
+        rank's logits (mib_row_logsumexp) gives each row's maximum, sum of exp(x - max) and target logit;
+        the ranks' partials combine as M = max, S = sum s exp(m - M), loss = log S + M - target."""
+        lo = self.lm_head.lo
+        V = logits.shape[-1]
+        x = logits.reshape(-1, V)
+        if x.stride(-1) != 1:
+            x = x.contiguous()
+        tgt_ids = target.reshape(-1).to(torch.int64).contiguous()
+        rows = x.shape[0]
+        lmax, sexp, tgt = (torch.empty(rows, dtype=torch.float32, device=x.device) for _ in range(3))
+        N.call("mib_row_logsumexp", N.ptr(x), rows, V, x.stride(0), N.ptr(tgt_ids), lo, N.ptr(lmax), N.ptr(sexp),
+               N.ptr(tgt), N.stream_ptr(x.device))
         if self.world > 1:
-            dist.all_reduce(lmax, op=dist.ReduceOp.MAX, group=self.group)
-        sexp = torch.exp(logits - lmax[..., None]).sum(-1)
-        local = (target >= lo) & (target < hi)
-        idx = (target - lo).clamp(0, hi - lo - 1)
-        tgt = torch.where(local, logits.gather(-1, idx[..., None])[..., 0], torch.zeros_like(lmax))
-        if self.world > 1:
+            gmax = lmax.clone()
+            dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=self.group)
+            sexp = sexp * torch.exp(lmax - gmax)
             dist.all_reduce(sexp, group=self.group)
             dist.all_reduce(tgt, group=self.group)
+            lmax = gmax
         return (torch.log(sexp) + lmax - tgt).mean()

@@ -122,3 +122,25 @@ def test_qk_norm_rope_bf16(hq, hk, d, cuda):
         step = (w16.float().abs() * 2.0 ** -7).clamp_min(1e-4)
         assert ((got.float() - w16.float()).abs() <= step).all()
         assert (got != w16).float().mean().item() <= 1e-2
+
+
+def test_row_logsumexp_matches_torch(cuda):
+    """mib_row_logsumexp (the Qwen3 driver's loss pass) against torch's fp32 logsumexp and gather, on a full
+    vocabulary row block and a shard of it with targets outside the shard."""
+    from memintelli_flash_b200 import _native as N
+    g = torch.Generator(device=cuda).manual_seed(4)
+    x = torch.randn(300, 151936, generator=g, device=cuda) * 3.0
+    t = torch.randint(0, 151936, (300,), generator=g, device=cuda)
+    for lo, hi in ((0, 151936), (40960, 60000)):
+        blk = x[:, lo:hi]
+        m, s, tg = (torch.empty(300, device=cuda) for _ in range(3))
+        N.call("mib_row_logsumexp", N.ptr(blk), 300, hi - lo, blk.stride(0), N.ptr(t), lo, N.ptr(m), N.ptr(s),
+               N.ptr(tg), N.stream_ptr(cuda))
+        torch.cuda.synchronize()
+        lse = torch.log(s) + m
+        ref = torch.logsumexp(blk.double(), dim=-1)
+        assert torch.allclose(lse.double(), ref, rtol=0, atol=2e-5)
+        assert torch.equal(m, blk.max(dim=-1).values)
+        inside = (t >= lo) & (t < hi)
+        want = torch.where(inside, blk.gather(1, (t - lo).clamp(0, hi - lo - 1)[:, None])[:, 0], torch.zeros_like(m))
+        assert torch.equal(tg, want)
