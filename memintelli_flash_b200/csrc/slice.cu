@@ -111,7 +111,7 @@ __device__ __forceinline__ int quantize_fast(float v, float bmax, int e, float i
 // Per-CTA table: packed code q -> encoded level of every slice.  E4M3 keeps slice t in byte t&3 of
 // word t>>2; FP16 keeps it in half t&1 of word t>>1.
 template <int KIND>
-struct LevelLut {
+struct alignas(16) LevelLut {
   static constexpr int kWords = KIND == MIB_OPERAND_E4M3 ? 2 : 4;
   uint32_t w[256][kWords];
 };
@@ -165,9 +165,11 @@ __device__ __forceinline__ void store_planes4(const LevelLut<KIND>& lut, const S
                                               int q1, int q2, int q3) {
   const int ns = S > 0 ? S : a.n_slices;
   if constexpr (KIND == MIB_OPERAND_E4M3) {
-    const uint32_t lo0 = lut.w[q0][0], lo1 = lut.w[q1][0], lo2 = lut.w[q2][0], lo3 = lut.w[q3][0];
-    uint32_t hi0 = 0, hi1 = 0, hi2 = 0, hi3 = 0;
-    if (S == 0 || S > 4) hi0 = lut.w[q0][1], hi1 = lut.w[q1][1], hi2 = lut.w[q2][1], hi3 = lut.w[q3][1];
+    // one 8-byte shared load per code: the encoded levels of all slices
+    const uint2 e0 = *reinterpret_cast<const uint2*>(lut.w[q0]), e1 = *reinterpret_cast<const uint2*>(lut.w[q1]);
+    const uint2 e2 = *reinterpret_cast<const uint2*>(lut.w[q2]), e3 = *reinterpret_cast<const uint2*>(lut.w[q3]);
+    const uint32_t lo0 = e0.x, lo1 = e1.x, lo2 = e2.x, lo3 = e3.x;
+    const uint32_t hi0 = e0.y, hi1 = e1.y, hi2 = e2.y, hi3 = e3.y;
     uint8_t* base = static_cast<uint8_t*>(a.planes) + dst;
 #pragma unroll
     for (int t = 0; t < (S > 0 ? S : 8); ++t) {
@@ -180,14 +182,19 @@ __device__ __forceinline__ void store_planes4(const LevelLut<KIND>& lut, const S
     }
   } else {
     __half* base = static_cast<__half*>(a.planes) + dst;
+    // one 16-byte shared load per code: the FP16 levels of all slices
+    const uint4 e0 = *reinterpret_cast<const uint4*>(lut.w[q0]), e1 = *reinterpret_cast<const uint4*>(lut.w[q1]);
+    const uint4 e2 = *reinterpret_cast<const uint4*>(lut.w[q2]), e3 = *reinterpret_cast<const uint4*>(lut.w[q3]);
+    const uint32_t w0[4] = {e0.x, e0.y, e0.z, e0.w}, w1[4] = {e1.x, e1.y, e1.z, e1.w};
+    const uint32_t w2[4] = {e2.x, e2.y, e2.z, e2.w}, w3[4] = {e3.x, e3.y, e3.z, e3.w};
 #pragma unroll
     for (int t = 0; t < (S > 0 ? S : 8); ++t) {
       if (S == 0 && t >= ns) break;
       const int wk = t >> 1;
       const uint32_t sel = (t & 1) ? 0x7632u : 0x5410u;
       uint2 o;
-      o.x = __byte_perm(lut.w[q0][wk], lut.w[q1][wk], sel);
-      o.y = __byte_perm(lut.w[q2][wk], lut.w[q3][wk], sel);
+      o.x = __byte_perm(w0[wk], w1[wk], sel);
+      o.y = __byte_perm(w2[wk], w3[wk], sel);
       if (a.vnoise != 0.0f) o = vnoise4(o, a, t * a.plane_stride + dst);
       *reinterpret_cast<uint2*>(base + t * a.plane_stride) = o;
     }
@@ -294,6 +301,43 @@ __device__ __forceinline__ int quantize_vec(float v, float bmax, float rb, float
     q = bmax == 0.0f ? 0 : rne_small(__fmul_rn(__fdiv_rn(v, bmax), qmax));
   }
   return q & ((1 << bits) - 1);
+}
+
+// Packed fp32 pairs (sm_100 f32x2 instructions): the same IEEE operation on both lanes.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ uint64_t fmul2_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2_rn(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t ffma2_rn(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// The INT branch of quantize_vec (rb != 0) on two values at once: div_markstein, the multiply by qmax and
+// rne_small with the identical IEEE steps per lane, as packed f32x2 operations.
+__device__ __forceinline__ void quantize2_int(float v0, float v1, float bmax, float rb, float qmax, int bits, int& q0,
+                                              int& q1) {
+  const uint64_t v = f2pack(v0, v1), r2 = f2pack(rb, rb), nb = f2pack(-bmax, -bmax);
+  uint64_t y = fmul2_rn(v, r2);
+  uint64_t r = ffma2_rn(nb, y, v);
+  y = ffma2_rn(r, r2, y);
+  r = ffma2_rn(nb, y, v);
+  y = ffma2_rn(r, r2, y);
+  y = fmul2_rn(y, f2pack(qmax, qmax));
+  y = fadd2_rn(y, f2pack(12582912.0f, 12582912.0f));
+  const int mask = (1 << bits) - 1;
+  q0 = (static_cast<int>(static_cast<uint32_t>(y)) - 0x4B400000) & mask;
+  q1 = (static_cast<int>(static_cast<uint32_t>(y >> 32)) - 0x4B400000) & mask;
 }
 
 // Element sources of the vector kernel.  row(b, r) prepares a per-row context once per work item;
@@ -434,6 +478,7 @@ __global__ void __launch_bounds__(256, 4) slice_vec_kernel(Src src, SliceArgs a,
   const int glanes = a.qg1 <= 128 ? a.qg1 / 4 : 32;
   const int leader = lane & ~(glanes - 1);
   const float qmax = static_cast<float>((1 << (a.bits - 1)) - 1);
+  const float inv_qmax = 1.0f / qmax;
   for (int item = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; item < nitems; item += nwarps) {
     const int row_idx = item / ngroups;
     const int ch0 = (item - row_idx * ngroups) * kSliceVecChunks;
@@ -469,7 +514,7 @@ __global__ void __launch_bounds__(256, 4) slice_vec_kernel(Src src, SliceArgs a,
         e = __shfl_sync(0xffffffffu, e, leader);
         scale = pow2f(e + 2 - a.bits);
       } else {
-        scale = bm / qmax;
+        scale = __fmul_rn(bm, inv_qmax);   // dequantisation factor (within one ulp of bm / qmax)
         if (bm >= 0x1p-60f && bm < 0x1p126f) rb = __frcp_rn(bm);
       }
       if (!valid) continue;
@@ -479,10 +524,16 @@ __global__ void __launch_bounds__(256, 4) slice_vec_kernel(Src src, SliceArgs a,
       }
       if ((col & (a.p - 1)) == 0) a.tile_scale[static_cast<int64_t>(col >> lp) * a.scale_ld + row_idx] = scale;
       const float inv_p2e = (a.bfp && e <= 126) ? pow2f(-e) : 0.0f;
-      const int q0 = quantize_vec(v[u].x, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-      const int q1 = quantize_vec(v[u].y, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-      const int q2 = quantize_vec(v[u].z, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-      const int q3 = quantize_vec(v[u].w, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      int q0, q1, q2, q3;
+      if (!a.bfp && rb != 0.0f) {
+        quantize2_int(v[u].x, v[u].y, bm, rb, qmax, a.bits, q0, q1);
+        quantize2_int(v[u].z, v[u].w, bm, rb, qmax, a.bits, q2, q3);
+      } else {
+        q0 = quantize_vec(v[u].x, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+        q1 = quantize_vec(v[u].y, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+        q2 = quantize_vec(v[u].z, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+        q3 = quantize_vec(v[u].w, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      }
       if (a.packed)
         *reinterpret_cast<uint32_t*>(a.packed + static_cast<int64_t>(row_idx) * kp + col) =
             static_cast<uint32_t>(q0) | (static_cast<uint32_t>(q1) << 8) | (static_cast<uint32_t>(q2) << 16) |

@@ -44,9 +44,13 @@ def _weight(device, bfp):
                       quant_gran=(128, 128), device=device, inference=True)
 
 
-def bench_slice(rows, cols, bfp=False, iters=20, device="cuda:0"):
+def bench_slice(rows, cols, bfp=False, iters=20, device="cuda:0", fp16=False):
+    """``fp16``: an engine whose only noise is read variation, which slices inputs straight into FP16 planes
+    (the Qwen3 benchmark's input path); else E4M3 planes."""
     dev = torch.device(device)
     eng = _engine(dev, False)
+    if fp16:
+        eng.read_variation = {i: 0.05 for i in range(eng.g_level)}
     x = torch.randn(rows, cols, device=dev)
     xs = _input(dev, bfp)
     for _ in range(3):
@@ -61,9 +65,10 @@ def bench_slice(rows, cols, bfp=False, iters=20, device="cuda:0"):
     torch.cuda.synchronize(dev)
     N.device_status()
     us = e0.elapsed_time(e1) * 1e3 / iters
-    nbytes = rows * cols * (4 + len(SLICES) + 4 / 32)
-    print(f"slice rows={rows} cols={cols} bfp={bfp}: {us:.1f} us/call, {nbytes / us / 1e3:.0f} GB/s algorithmic",
-          flush=True)
+    esz = xs._buf["planes"].element_size()
+    nbytes = rows * cols * (4 + esz * len(SLICES) + 4 / 32)
+    print(f"slice rows={rows} cols={cols} bfp={bfp} planes={'fp16' if esz == 2 else 'e4m3'}: {us:.1f} us/call, "
+          f"{nbytes / us / 1e3:.0f} GB/s algorithmic", flush=True)
     return us
 
 
@@ -284,6 +289,7 @@ def main(argv=None):
     s.add_argument("--cols", type=int, default=3072)
     s.add_argument("--bfp", action="store_true")
     s.add_argument("--iters", type=int, default=20)
+    s.add_argument("--fp16", action="store_true")
     v = sub.add_parser("mvm")
     v.add_argument("--m", type=int, default=4096)
     v.add_argument("--k", type=int, default=4096)
@@ -301,7 +307,7 @@ def main(argv=None):
     w.add_argument("--iters", type=int, default=5)
     a = ap.parse_args(argv)
     if a.kernel == "slice":
-        bench_slice(a.rows, a.cols, a.bfp, a.iters)
+        bench_slice(a.rows, a.cols, a.bfp, a.iters, fp16=a.fp16)
     elif a.kernel == "mvm":
         bench_mvm(a.m, a.k, a.n, a.noisy, a.bfp, a.iters)
     elif a.kernel == "noise":

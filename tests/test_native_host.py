@@ -196,3 +196,12 @@ def test_noisy_conv_slicing_and_failure_injection_check_arguments():
     assert L.mib_slice_conv_input_noisy(None, *args[1:], 0.05, 1, 0, None) == N.MIB_ERR_PARAM
     assert L.mib_test_inject_wait_expiry(0) == N.MIB_ERR_PARAM
     assert L.mib_test_inject_wait_expiry(5_000_000_000) == N.MIB_ERR_PARAM
+
+
+def test_row_logsumexp_checks_arguments():
+    L = N.lib()
+    fake = ctypes.c_void_p(0x1000)
+    assert L.mib_row_logsumexp(None, 4, 8, 8, None, 0, fake, fake, None, None) == N.MIB_ERR_PARAM
+    assert L.mib_row_logsumexp(fake, 4, 8, 8, None, 0, fake, fake, fake, None) == N.MIB_ERR_PARAM   # targets needed
+    assert L.mib_row_logsumexp(fake, 4, 8, 6, None, 0, fake, fake, None, None) == N.MIB_ERR_SHAPE   # ld < cols
+    assert L.mib_row_logsumexp(fake, 0, 8, 8, None, 0, fake, fake, None, None) == N.MIB_ERR_SHAPE
