@@ -261,11 +261,15 @@ int adc_plan(const SliceTab& tx, const SliceTab& tw, const mib_slice_spec* xs, c
   const bool exact = noise_free(dev);
   bool need_lut = false;
   if (exact) {
-    // magic-constant rounding must reproduce the exact half-even code for every reachable S in [0, D]
+    // magic-constant rounding must reproduce the exact half-even code for every reachable S in [0, D], both
+    // as one fused multiply-add and as a rounded product followed by a rounded add, so that the result
+    // does not depend on how the packed f32x2 instruction evaluates it
     for (int j = 0; j < tw.S && !need_lut; ++j) {
       for (long long S = 0; S <= D; ++S) {
         const float t = std::fma(static_cast<float>(S), pl.cadc[j], 12582912.0f) - 12582912.0f;
-        if (static_cast<long long>(t) != rne_div(S * pl.R[j], D)) {
+        volatile float prod = static_cast<float>(S) * pl.cadc[j];
+        const float t2 = (prod + 12582912.0f) - 12582912.0f;
+        if (static_cast<long long>(t) != rne_div(S * pl.R[j], D) || static_cast<long long>(t2) != rne_div(S * pl.R[j], D)) {
           need_lut = true;
           break;
         }

@@ -303,43 +303,6 @@ __device__ __forceinline__ int quantize_vec(float v, float bmax, float rb, float
   return q & ((1 << bits) - 1);
 }
 
-// Packed fp32 pairs (sm_100 f32x2 instructions): the same IEEE operation on both lanes.
-__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
-  return (static_cast<uint64_t>(__float_as_uint(hi)) << 32) | __float_as_uint(lo);
-}
-__device__ __forceinline__ uint64_t fmul2_rn(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t fadd2_rn(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
-__device__ __forceinline__ uint64_t ffma2_rn(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-
-// The INT branch of quantize_vec (rb != 0) on two values at once: div_markstein, the multiply by qmax and
-// rne_small with the identical IEEE steps per lane, as packed f32x2 operations.
-__device__ __forceinline__ void quantize2_int(float v0, float v1, float bmax, float rb, float qmax, int bits, int& q0,
-                                              int& q1) {
-  const uint64_t v = f2pack(v0, v1), r2 = f2pack(rb, rb), nb = f2pack(-bmax, -bmax);
-  uint64_t y = fmul2_rn(v, r2);
-  uint64_t r = ffma2_rn(nb, y, v);
-  y = ffma2_rn(r, r2, y);
-  r = ffma2_rn(nb, y, v);
-  y = ffma2_rn(r, r2, y);
-  y = fmul2_rn(y, f2pack(qmax, qmax));
-  y = fadd2_rn(y, f2pack(12582912.0f, 12582912.0f));
-  const int mask = (1 << bits) - 1;
-  q0 = (static_cast<int>(static_cast<uint32_t>(y)) - 0x4B400000) & mask;
-  q1 = (static_cast<int>(static_cast<uint32_t>(y >> 32)) - 0x4B400000) & mask;
-}
-
 // Element sources of the vector kernel.  row(b, r) prepares a per-row context once per work item;
 // load4(row, col) returns columns col..col+3 of that row, zero beyond the matrix.
 
@@ -524,16 +487,10 @@ __global__ void __launch_bounds__(256, 4) slice_vec_kernel(Src src, SliceArgs a,
       }
       if ((col & (a.p - 1)) == 0) a.tile_scale[static_cast<int64_t>(col >> lp) * a.scale_ld + row_idx] = scale;
       const float inv_p2e = (a.bfp && e <= 126) ? pow2f(-e) : 0.0f;
-      int q0, q1, q2, q3;
-      if (!a.bfp && rb != 0.0f) {
-        quantize2_int(v[u].x, v[u].y, bm, rb, qmax, a.bits, q0, q1);
-        quantize2_int(v[u].z, v[u].w, bm, rb, qmax, a.bits, q2, q3);
-      } else {
-        q0 = quantize_vec(v[u].x, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-        q1 = quantize_vec(v[u].y, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-        q2 = quantize_vec(v[u].z, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-        q3 = quantize_vec(v[u].w, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
-      }
+      const int q0 = quantize_vec(v[u].x, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      const int q1 = quantize_vec(v[u].y, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      const int q2 = quantize_vec(v[u].z, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
+      const int q3 = quantize_vec(v[u].w, bm, rb, qmax, e, inv_p2e, a.bits, a.bfp);
       if (a.packed)
         *reinterpret_cast<uint32_t*>(a.packed + static_cast<int64_t>(row_idx) * kp + col) =
             static_cast<uint32_t>(q0) | (static_cast<uint32_t>(q1) << 8) | (static_cast<uint32_t>(q2) << 16) |
