@@ -82,6 +82,10 @@ class DPETensor(object):
         # Device on which the fixed-seed fault fields are drawn; None = the weight's device,
         # as in the reference.  Tests set "cpu" to reproduce a CPU reference run's faults.
         self.fault_field_device = None
+        # Conv2dMem: apply the voltage noise inside the conv-patch slicing instead of a separate pass over the
+        # planes (same values).  Off by default: on the ResNet-18-CIFAR layer stack the slicing kernel with the
+        # Philox draws inside measured slower than slicing plus the separate pass.
+        self.fuse_conv_input_noise = False
         self._plans = {}
         self._ws_floats = {}
         # When a list, every fused MVM launch appends (start_event, end_event, slice_pair_ops,
@@ -229,9 +233,9 @@ class DPETensor(object):
 
     def conv_input_noise_fused(self) -> bool:
         """Whether a convolution input sliced once per multiply (Conv2dMem) gets this call's voltage noise
-        inside the slicing: E4M3-sized levels with voltage noise on.  The multiply then skips its
-        separate noise pass; the values are the same."""
-        return self.vnoise > 0 and self.operand_kind == N.OPERAND_E4M3
+        inside the slicing (``fuse_conv_input_noise``, E4M3-sized levels, voltage noise on).  The multiply
+        then skips its separate noise pass; the values are the same bit for bit."""
+        return self.fuse_conv_input_noise and self.vnoise > 0 and self.operand_kind == N.OPERAND_E4M3
 
     def _slice_conv_input(self, sd: SlicedData, x: torch.Tensor, kernel_size, stride, padding, dilation,
                           noise_seed=None):

@@ -177,3 +177,52 @@ def test_bench_engine_forward_is_deterministic_per_seed(cuda):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert not torch.equal(a, c)
+
+
+def test_resnet18_cifar_stage1_conv_matches_oracle(cuda):
+    """Config 2 at full size: a ResNet-18-CIFAR stage-1 conv (64 -> 64 channels, 3x3, padding 1) on 128 images of
+    30x30, block floating point (bw_e 8), radc 1024 (the per-slice code-table ADC), x (1,64)/(1,32),
+    W (64,64)/(32,32): 115200 output pixels x 576 patch columns, sliced straight from NCHW.  Rows are output
+    pixels; 128 of them, spread over all images, equal the oracle on F.unfold's columns."""
+    import torch.nn.functional as F
+    import memintelli_flash_b200 as M_
+    from memintelli_flash_b200.NN_layers import Conv2dMem
+    eng = M_.DPETensor(device=cuda, **dict(NOISE_FREE, radc=1024))
+    torch.manual_seed(2)
+    layer = Conv2dMem(eng, 64, 64, 3, SM, SM, stride=1, padding=1, bias=False, device=cuda, bw_e=8,
+                      input_paral_size=(1, 32), weight_paral_size=(32, 32), input_quant_gran=(1, 64),
+                      weight_quant_gran=(64, 64))
+    layer.inference_mode = True
+    g = torch.Generator(device=cuda).manual_seed(3)
+    x = torch.randn(128, 64, 30, 30, generator=g, device=cuda)
+    y = layer(x)                                                  # (128, 64, 30, 30)
+    torch.cuda.synchronize()
+    rows = _rows(128 * 900)
+    xu = F.unfold(x, 3, padding=1).transpose(1, 2).reshape(-1, 576)[torch.from_numpy(rows).to(cuda)]
+    wm = layer.weight.detach().reshape(64, -1).t().contiguous()
+    oxs = O.slice_matrix(xu.cpu().numpy(), SM, 8, (1, 32), (1, 64))
+    ows = O.slice_matrix(wm.cpu().numpy(), SM, 8, (32, 32), (64, 64))
+    ref = O.mvm_exact(oxs, ows, O.Engine(**dict(NOISE_FREE, radc=1024)))
+    got = y.permute(0, 2, 3, 1).reshape(-1, 64)[torch.from_numpy(rows).to(cuda)].double().cpu().numpy()
+    _check(got, ref)
+
+
+def test_deit_small_qkv_k64_matches_oracle(cuda):
+    """Config 3 at full size: the DeiT-S q/k/v crossbar (384 -> 1152) over 64 x 197 = 12608 tokens with 64-deep
+    crossbar tiles (x (1,64)/(1,64), W (64,64)/(64,64)), INT, radc 4096, noise-free."""
+    import memintelli_flash_b200 as M_
+    eng = M_.DPETensor(device=cuda, **NOISE_FREE)
+    x, w = _inputs(12608, 384, 1152, seed=21)
+    xs = M_.SlicedData(torch.tensor(SM), is_weight=False, paral_size=(1, 64), quant_gran=(1, 64), device=cuda,
+                       inference=True)
+    ws = M_.SlicedData(torch.tensor(SM), is_weight=True, paral_size=(64, 64), quant_gran=(64, 64), device=cuda,
+                       inference=True)
+    ws.slice_data_imp(eng, w.to(cuda))
+    xs.slice_data_imp(eng, x.to(cuda))
+    y = eng(xs, ws)
+    torch.cuda.synchronize()
+    rows = _rows(12608, n=97)
+    oxs = O.slice_matrix(x[rows].numpy(), SM, None, (1, 64), (1, 64))
+    ows = O.slice_matrix(w.numpy(), SM, None, (64, 64), (64, 64))
+    ref = O.mvm_exact(oxs, ows, O.Engine(**NOISE_FREE))
+    _check(y[torch.from_numpy(rows).to(cuda)].double().cpu().numpy(), ref)

@@ -106,6 +106,8 @@ def test_conv_voltage_noise_fused_into_slicing_equals_separate_pass(bfp, cuda):
     from memintelli_flash_b200.NN_layers import Conv2dMem
     eng = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=1024, write_variation=0.0,
                       rate_stuck_HGS=0.0, rate_stuck_LGS=0.0, read_variation=0.05, vnoise=0.05)
+    assert not eng.conv_input_noise_fused()          # opt-in
+    eng.fuse_conv_input_noise = True
     assert eng.conv_input_noise_fused()
     torch.manual_seed(3)
     layer = Conv2dMem(eng, 16, 32, 3, [1, 1, 2, 2, 2], [1, 1, 2, 2, 2], stride=1, padding=1, bias=True,
