@@ -12,6 +12,8 @@
 // memory, so B is one K-major operand of Sy*BN rows and the accumulator is a
 // 128 x (Sy*BN) fp32 block of tensor memory.  Two such slots alternate.
 //
+// Launches without split-K are persistent: 148 CTAs (one per SM) step through the output tiles.
+//
 // Warp roles (one CTA per SM):
 //   warps 0 .. 4*CG-1  epilogue: warp w reads TMEM lanes 32*(w%4).. (its rows) and
 //                      columns 16*(w/4).. of every weight slice; ADC, shift-add,
@@ -99,8 +101,20 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   int32_t* lut_s = reinterpret_cast<int32_t*>(ctl + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * kMvmBM;
-  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * BN;
+  // Persistent (launches without split-K): CTA b processes output tiles b, b + grid, ... (column tiles
+  // fastest).  The stage ring, the TMEM slots and the barrier phases run on across tiles, so the next
+  // tile's loads and MMAs proceed while this tile's outputs are stored (measured 1.8-2.0% faster on
+  // 16384-row K = 1024 arrays, equal on 4096^3).
+  constexpr bool kPersist = !SPLIT;
+  const int64_t n_tiles_n = (P.N + BN - 1) / BN;
+  const int64_t n_tiles = n_tiles_n * ((P.M + kMvmBM - 1) / kMvmBM);
+  const int64_t my_tiles = kPersist ? (n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 1;
+  auto tile_m0 = [&](int64_t jt) -> int64_t {
+    return kPersist ? ((blockIdx.x + jt * gridDim.x) / n_tiles_n) * kMvmBM : static_cast<int64_t>(blockIdx.y) * kMvmBM;
+  };
+  auto tile_n0 = [&](int64_t jt) -> int64_t {
+    return kPersist ? ((blockIdx.x + jt * gridDim.x) % n_tiles_n) * BN : static_cast<int64_t>(blockIdx.x) * BN;
+  };
   constexpr int Sy = SY;
   const int Sx = SXC > 0 ? SXC : P.Sx;
   const int stages = P.stages;
@@ -141,26 +155,37 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     if (lane == 0) {
       tma_prefetch_desc(&tma_a);
       tma_prefetch_desc(&tma_b);
-      int issued = 0;
+      int64_t issued = 0;
       int s = 0;
       uint32_t phase = 0;
-      for (int t = 0; t < Kt; ++t) {
-        if (t >= stages && !mbar_wait(&ctl->empty[s], phase ^ 1u, abort, 11, P.wait_limit)) break;
+      const int64_t steps = my_tiles * Kt;
+      int64_t jt = 0;   // tile of this CTA and K tile inside it, stepped along with g (no division)
+      int t = 0;
+      int tm0 = static_cast<int>(tile_m0(0)), tn0 = static_cast<int>(tile_n0(0));
+      for (int64_t g = 0; g < steps; ++g) {
+        if (g >= stages && !mbar_wait(&ctl->empty[s], phase ^ 1u, abort, 11, P.wait_limit)) break;
         uint8_t* a_dst = smem + static_cast<size_t>(s) * P.stage_bytes;
         uint8_t* b_dst = a_dst + static_cast<size_t>(Sx) * P.a_slice_bytes;
         mbar_arrive_expect_tx(&ctl->full[s], P.stage_bytes);
-        tma_load_3d(a_dst, &tma_a, &ctl->full[s], (t_begin + t) * P.pp, static_cast<int>(m0), 0);
-        tma_load_3d(b_dst, &tma_b, &ctl->full[s], (t_begin + t) * P.pp, static_cast<int>(n0), 0);
-        issued = t + 1;
+        tma_load_3d(a_dst, &tma_a, &ctl->full[s], (t_begin + t) * P.pp, tm0, 0);
+        tma_load_3d(b_dst, &tma_b, &ctl->full[s], (t_begin + t) * P.pp, tn0, 0);
+        issued = g + 1;
         if (++s == stages) {
           s = 0;
           phase ^= 1u;
         }
+        if (++t == Kt) {
+          t = 0;
+          if (++jt < my_tiles) {
+            tm0 = static_cast<int>(tile_m0(jt));
+            tn0 = static_cast<int>(tile_n0(jt));
+          }
+        }
       }
       // no TMA write may still be in flight when the CTA exits
-      const int first = issued > stages ? issued - stages : 0;
-      for (int t = first; t < issued; ++t)
-        mbar_wait_drain(&ctl->full[t % stages], static_cast<uint32_t>(t / stages) & 1u, 12);
+      const int64_t first = issued > stages ? issued - stages : 0;
+      for (int64_t g = first; g < issued; ++g)
+        mbar_wait_drain(&ctl->full[g % stages], static_cast<uint32_t>(g / stages) & 1u, 12);
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------------ MMA
@@ -170,7 +195,8 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       int slot = 0, s = 0, uses = 0;
       uint32_t sphase = 0, tphase = 0;
       bool ok = P.hold_mma == 0;   // held (test hook): no MMA and no commit, the epilogue's wait runs out
-      for (int t = 0; t < Kt && ok; ++t) {
+      const int64_t steps = my_tiles * Kt;
+      for (int64_t g = 0; g < steps && ok; ++g) {
         if (!mbar_wait(&ctl->full[s], sphase, abort, 21, P.wait_limit)) {
           ok = false;
           break;
@@ -211,7 +237,6 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     // ------------------------------------------------------------- epilogue
     const int q = warp & 3;             // TMEM lane quarter this warp may access
     const int cg = (warp >> 2) * 16;    // 16-column group inside each weight slice's BN columns
-    const int64_t row = m0 + q * 32 + lane;
     const uint32_t lane_addr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + cg;
     // ADC constants (radc_j - 1) / D, duplicated into f32x2 pairs, and the rounding constant pair
     uint64_t cj2[SY];
@@ -229,7 +254,16 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     int slot = 0, cnt = 0;
     uint32_t tphase = 0;
     bool ok = true;
-    for (int t = 0; t < Kt && ok; ++t) {
+    const int64_t steps = my_tiles * Kt;
+    int64_t m0 = tile_m0(0), n0 = tile_n0(0);
+    int64_t row = m0 + q * 32 + lane;
+    int64_t jt = 0;   // tile of this CTA
+    int t = -1;       // K tile inside it
+    for (int64_t g = 0; g < steps && ok; ++g) {
+      if (++t == Kt) {
+        t = 0;
+        ++jt;
+      }
 #pragma unroll kSxUnroll
       for (int i = 0; i < Sx; ++i) {
         if (!warp_wait(&ctl->tfull[slot], tphase, abort, 31, P.wait_limit)) {
@@ -322,8 +356,29 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
         }
         cnt = 0;
       }
+      if (kPersist && t == Kt - 1) {
+        if (row < P.M) {
+          const int64_t grp = row / P.rows_per_group;
+          const int64_t rr = row - grp * P.rows_per_group;
+          float* yb = P.y + grp * P.group_stride + rr * P.row_stride;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int64_t n = n0 + cg + c;
+            if (n < P.N) yb[n * P.col_stride] = out[c] + (P.bias ? __ldg(P.bias + n) : 0.0f);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 16; ++c) out[c] = 0.0f;
+        if (jt + 1 < my_tiles) {
+          m0 = tile_m0(jt + 1);
+          n0 = tile_n0(jt + 1);
+          row = m0 + q * 32 + lane;
+        }
+      }
     }
-    if (SPLIT && ok && row < P.M) {
+    if (kPersist) {
+      // every tile was stored inside the loop
+    } else if (SPLIT && ok && row < P.M) {
       float* pr = P.partial + (static_cast<int64_t>(blockIdx.z) * P.M + row) * P.N;
 #pragma unroll
       for (int c = 0; c < 16; ++c) {
@@ -370,6 +425,17 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const MvmAr
   constexpr int BN = 16 * CG;
   const unsigned splits = SPLIT ? static_cast<unsigned>((a.Kt + a.tiles_per_split - 1) / a.tiles_per_split) : 1u;
   dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + kMvmBM - 1) / kMvmBM), splits);
+  if (!SPLIT) {   // persistent: one CTA per SM (at most one fits, by shared memory)
+    static std::atomic<int> sm_count[128] = {};
+    int sms = sm_count[device].load(std::memory_order_relaxed);
+    if (sms == 0) {
+      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      if (e != cudaSuccess) return e;
+      sm_count[device].store(sms, std::memory_order_relaxed);
+    }
+    const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y;
+    grid = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms), 1, 1);
+  }
   fn<<<grid, 32 * (4 * CG + 2), smem, stream>>>(ta, tb, a);
   count_launch();
   return cudaGetLastError();
