@@ -91,6 +91,14 @@ struct MvmArgs {
   int32_t* acc_dump;        // [Kt][M][N] or null
   int32_t tiles_per_split;  // K tiles per CTA along grid z (== Kt without split-K)
   float* partial;           // split-K: [splits][M][N] fp32 partial outputs, or null
+  // Persistent launches (no split-K): output tiles [0, dp_tiles) are stepped whole, CTA b taking tiles
+  // b, b + grid, ...  With tail_splits > 1 the remaining tiles (a partly idle last wave) are cut into
+  // tail_splits K ranges of tail_tiles_per_split K tiles; CTA b takes range b % tail_splits of tile
+  // dp_tiles + b / tail_splits and writes it to tail_partial[b][128][BN], summed by tail_reduce.
+  int64_t dp_tiles;
+  int32_t tail_splits;
+  int32_t tail_tiles_per_split;
+  float* tail_partial;
   int64_t wait_limit;       // cycles after which an abortable mbarrier wait gives up (about 2 s normally)
   int32_t hold_mma;         // test hook: the MMA warp issues nothing, so the epilogue's first wait runs out
 };
@@ -120,6 +128,11 @@ cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, in
                                  int64_t rows_per_group, int64_t group_stride, int64_t row_stride,
                                  int64_t col_stride, const float* bias, cudaStream_t stream);
 int mvm_column_groups(int sy);   // output tile width BN = 16 * mvm_column_groups(Sy)
+cudaError_t launch_tail_reduce(const float* tail_partial, int splits, int64_t dp_tiles, int64_t tail_tiles, int bn,
+                               int64_t M, int64_t N, float* y, int64_t rows_per_group, int64_t group_stride,
+                               int64_t row_stride, int64_t col_stride, const float* bias, cudaStream_t stream);
+// Multiprocessor count of `device`, cached per device.
+cudaError_t device_sm_count(int device, int* sms);
 cudaError_t launch_mvm(const CUtensorMap& ta, const CUtensorMap& tb, const MvmArgs& a, int kind, int acc_mode,
                        cudaStream_t stream);
 

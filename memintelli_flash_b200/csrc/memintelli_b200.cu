@@ -352,6 +352,51 @@ SplitPlan split_plan(int64_t m, int64_t n, int64_t kt, int flush, int sy, bool b
   return best_cost <= 0.9 * unsplit ? best : split_ranges(kt, flush, groups, 1);
 }
 
+// Tail split of a persistent launch: when the last wave of output tiles fills at most half of the
+// SMs, those tiles are cut into K ranges (whole flush groups) so that the wave's work is spread over
+// all SMs; tail_reduce adds the ranges in K order.  For example 2816 tiles on 148 SMs take 20 waves,
+// the last one 4 tiles; cut into 16 ranges each, they take 1/16 of a wave.
+struct TailPlan {
+  int64_t dp_tiles = 0;   // tiles stepped whole
+  int splits = 1;         // K ranges per tail tile (1: no tail split)
+  int tiles_per_split = 0;
+  int64_t floats = 0;     // partial outputs: tail tiles x splits x 128 x BN
+};
+
+TailPlan tail_plan(int64_t m, int64_t n, int64_t kt, int flush, int sy, int sms) {
+  TailPlan tp;
+  const int64_t bn = 16 * mib::mvm_column_groups(sy);
+  const int64_t tiles = ((n + bn - 1) / bn) * ((m + mib::kMvmBM - 1) / mib::kMvmBM);
+  tp.dp_tiles = tiles;
+  if (sms < 2 || tiles <= sms) return tp;
+  const int64_t waves = (tiles + sms - 1) / sms;
+  const int64_t rem = tiles - (waves - 1) * sms;
+  const int64_t groups = (kt + flush - 1) / flush;
+  if (2 * rem > sms || groups < 2) return tp;
+  const SplitPlan sp = split_ranges(kt, flush, groups, sms / rem);
+  if (sp.splits < 2) return tp;
+  tp.dp_tiles = (waves - 1) * sms;
+  tp.splits = sp.splits;
+  tp.tiles_per_split = sp.tiles_per_split;
+  tp.floats = rem * sp.splits * mib::kMvmBM * bn;
+  return tp;
+}
+
+// Multiprocessor count of the current device.  A workspace query made where no CUDA device is
+// visible (planning on a host without a GPU) plans for a B200's 148 SMs.
+int current_sm_count(int* sms) {
+  int device = 0, count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0) {
+    cudaGetLastError();
+    *sms = 148;
+    return MIB_OK;
+  }
+  cudaError_t e = cudaGetDevice(&device);
+  if (e == cudaSuccess) e = mib::device_sm_count(device, sms);
+  if (e != cudaSuccess) return cuda_fail(e, "multiprocessor count");
+  return MIB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -665,6 +710,11 @@ static int split_workspace_floats(int64_t m, int64_t n, const mib_slice_spec* x_
   if (int r = adc_plan(tx, tw, x_spec, w_spec, kg, dev, pl)) return r;
   const SplitPlan sp = split_plan(m, n, kg->kt, pl.flush, tw.S, balance);
   *floats_out = sp.splits > 1 ? static_cast<int64_t>(sp.splits) * m * n : 0;
+  if (balance && sp.splits == 1) {
+    int sms = 0;
+    if (int r = current_sm_count(&sms)) return r;
+    *floats_out = tail_plan(m, n, kg->kt, pl.flush, tw.S, sms).floats;
+  }
   return MIB_OK;
 }
 
@@ -753,6 +803,17 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
     sp = SplitPlan{1, static_cast<int>(kg->kt)};
   a.tiles_per_split = sp.tiles_per_split;
   a.partial = sp.splits > 1 ? workspace : nullptr;
+  TailPlan tl = tail_plan(m, n, kg->kt, pl.flush, tw.S, 0);   // no tail split: dp_tiles = every tile
+  if (sp.splits == 1 && workspace) {
+    int sms = 0;
+    if (int r = current_sm_count(&sms)) return r;
+    const TailPlan t2 = tail_plan(m, n, kg->kt, pl.flush, tw.S, sms);
+    if (t2.splits > 1 && workspace_floats >= t2.floats) tl = t2;
+  }
+  a.dp_tiles = tl.dp_tiles;
+  a.tail_splits = tl.splits;
+  a.tail_tiles_per_split = tl.tiles_per_split;
+  a.tail_partial = tl.splits > 1 ? workspace : nullptr;
   a.wait_limit = mib::kWaitTimeoutCycles;
   if (g_inject_wait_limit > 0) {
     a.wait_limit = g_inject_wait_limit;
@@ -768,6 +829,12 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
     e = mib::launch_splitk_reduce(a.partial, sp.splits, m, n, y, a.rows_per_group, a.group_stride, a.row_stride,
                                   a.col_stride, bias, stream);
     if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
+  }
+  if (a.tail_partial) {
+    const int64_t tiles = ((n + bn - 1) / bn) * ((m + mib::kMvmBM - 1) / mib::kMvmBM);
+    e = mib::launch_tail_reduce(a.tail_partial, tl.splits, tl.dp_tiles, tiles - tl.dp_tiles, bn, m, n, y,
+                                a.rows_per_group, a.group_stride, a.row_stride, a.col_stride, bias, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "tail reduce launch");
   }
   return MIB_OK;
 }

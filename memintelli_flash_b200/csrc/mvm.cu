@@ -103,17 +103,25 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // Persistent (launches without split-K): CTA b processes output tiles b, b + grid, ... (column tiles
   // fastest).  The stage ring, the TMEM slots and the barrier phases run on across tiles, so the next
-  // tile's loads and MMAs proceed while this tile's outputs are stored (measured 1.8-2.0% faster on
-  // 16384-row K = 1024 arrays, equal on 4096^3).
+  // tile's loads and MMAs proceed while this tile's outputs are stored.  The CTA's work is a list of
+  // items: its whole tiles below dp_tiles, then at most one K range of a tail tile (see MvmArgs).
   constexpr bool kPersist = !SPLIT;
   const int64_t n_tiles_n = (P.N + BN - 1) / BN;
   const int64_t n_tiles = n_tiles_n * ((P.M + kMvmBM - 1) / kMvmBM);
-  const int64_t my_tiles = kPersist ? (n_tiles - blockIdx.x + gridDim.x - 1) / gridDim.x : 1;
-  auto tile_m0 = [&](int64_t jt) -> int64_t {
-    return kPersist ? ((blockIdx.x + jt * gridDim.x) / n_tiles_n) * kMvmBM : static_cast<int64_t>(blockIdx.y) * kMvmBM;
+  const int64_t bx = blockIdx.x;
+  const int64_t my_dp = kPersist ? (P.dp_tiles > bx ? (P.dp_tiles - bx + gridDim.x - 1) / gridDim.x : 0) : 1;
+  const int tail_s = kPersist ? P.tail_splits : 0;
+  const bool has_tail = kPersist && tail_s > 1 && bx < (n_tiles - P.dp_tiles) * tail_s;
+  const int n_items_tail = has_tail ? 1 : 0;
+  const int64_t n_items = my_dp + n_items_tail;
+  auto item_tile = [&](int64_t it) -> int64_t {   // linear output tile of item `it` (persistent)
+    return it < my_dp ? bx + it * gridDim.x : P.dp_tiles + bx / tail_s;
   };
-  auto tile_n0 = [&](int64_t jt) -> int64_t {
-    return kPersist ? ((blockIdx.x + jt * gridDim.x) % n_tiles_n) * BN : static_cast<int64_t>(blockIdx.x) * BN;
+  auto tile_m0 = [&](int64_t it) -> int64_t {
+    return kPersist ? (item_tile(it) / n_tiles_n) * kMvmBM : static_cast<int64_t>(blockIdx.y) * kMvmBM;
+  };
+  auto tile_n0 = [&](int64_t it) -> int64_t {
+    return kPersist ? (item_tile(it) % n_tiles_n) * BN : static_cast<int64_t>(blockIdx.x) * BN;
   };
   constexpr int Sy = SY;
   const int Sx = SXC > 0 ? SXC : P.Sx;
@@ -122,6 +130,12 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   // split-K: this CTA covers K tiles [t_begin, t_begin + Kt)
   const int t_begin = SPLIT ? static_cast<int>(blockIdx.z) * P.tiles_per_split : 0;
   const int Kt = SPLIT ? min(P.tiles_per_split, static_cast<int>(P.Kt) - t_begin) : static_cast<int>(P.Kt);
+  // K tiles [item_lo, item_hi) of item `it`
+  const int tail_lo = has_tail ? static_cast<int>(bx % tail_s) * P.tail_tiles_per_split : 0;
+  const int tail_hi = has_tail ? min(Kt, tail_lo + P.tail_tiles_per_split) : 0;
+  auto item_lo = [&](int64_t it) -> int { return it < my_dp ? 0 : tail_lo; };
+  auto item_hi = [&](int64_t it) -> int { return it < my_dp ? Kt : tail_hi; };
+  const int64_t steps = my_dp * Kt + (tail_hi - tail_lo);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -158,9 +172,8 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       int64_t issued = 0;
       int s = 0;
       uint32_t phase = 0;
-      const int64_t steps = my_tiles * Kt;
-      int64_t jt = 0;   // tile of this CTA and K tile inside it, stepped along with g (no division)
-      int t = 0;
+      int64_t it = 0;   // item of this CTA and K tile inside it, stepped along with g (no division)
+      int t = item_lo(0), hi = item_hi(0);
       int tm0 = static_cast<int>(tile_m0(0)), tn0 = static_cast<int>(tile_n0(0));
       for (int64_t g = 0; g < steps; ++g) {
         if (g >= stages && !mbar_wait(&ctl->empty[s], phase ^ 1u, abort, 11, P.wait_limit)) break;
@@ -174,12 +187,11 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
           s = 0;
           phase ^= 1u;
         }
-        if (++t == Kt) {
-          t = 0;
-          if (++jt < my_tiles) {
-            tm0 = static_cast<int>(tile_m0(jt));
-            tn0 = static_cast<int>(tile_n0(jt));
-          }
+        if (++t == hi && ++it < n_items) {
+          t = item_lo(it);
+          hi = item_hi(it);
+          tm0 = static_cast<int>(tile_m0(it));
+          tn0 = static_cast<int>(tile_n0(it));
         }
       }
       // no TMA write may still be in flight when the CTA exits
@@ -195,7 +207,6 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       int slot = 0, s = 0, uses = 0;
       uint32_t sphase = 0, tphase = 0;
       bool ok = P.hold_mma == 0;   // held (test hook): no MMA and no commit, the epilogue's wait runs out
-      const int64_t steps = my_tiles * Kt;
       for (int64_t g = 0; g < steps && ok; ++g) {
         if (!mbar_wait(&ctl->full[s], sphase, abort, 21, P.wait_limit)) {
           ok = false;
@@ -254,16 +265,11 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
     int slot = 0, cnt = 0;
     uint32_t tphase = 0;
     bool ok = true;
-    const int64_t steps = my_tiles * Kt;
     int64_t m0 = tile_m0(0), n0 = tile_n0(0);
     int64_t row = m0 + q * 32 + lane;
-    int64_t jt = 0;   // tile of this CTA
-    int t = -1;       // K tile inside it
+    int64_t it = 0;                          // item of this CTA
+    int t = item_lo(0), hi = item_hi(0);     // K tile inside it, and its end
     for (int64_t g = 0; g < steps && ok; ++g) {
-      if (++t == Kt) {
-        t = 0;
-        ++jt;
-      }
 #pragma unroll kSxUnroll
       for (int i = 0; i < Sx; ++i) {
         if (!warp_wait(&ctl->tfull[slot], tphase, abort, 31, P.wait_limit)) {
@@ -331,7 +337,7 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
       }
       if (!ok) break;
       ++cnt;
-      if (kDump || cnt == P.flush_tiles || t == Kt - 1) {
+      if (kDump || cnt == P.flush_tiles || t == hi - 1) {
         const int tg = t_begin + t;   // global K tile
         const float xsv = row < P.M ? __ldg(P.xs + static_cast<int64_t>(tg) * P.M + row) : 0.0f;
         const float rs = kFloatAcc ? xsv : xsv * P.out_scale;
@@ -356,8 +362,13 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
         }
         cnt = 0;
       }
-      if (kPersist && t == Kt - 1) {
-        if (row < P.M) {
+      if (kPersist && t == hi - 1) {
+        if (it >= my_dp) {
+          // a K range of a tail tile: the whole 128 x BN partial, summed by tail_reduce
+          float* pt = P.tail_partial + (bx * kMvmBM + q * 32 + lane) * BN + cg;
+#pragma unroll
+          for (int c = 0; c < 16; ++c) pt[c] = out[c];
+        } else if (row < P.M) {
           const int64_t grp = row / P.rows_per_group;
           const int64_t rr = row - grp * P.rows_per_group;
           float* yb = P.y + grp * P.group_stride + rr * P.row_stride;
@@ -369,11 +380,15 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
         }
 #pragma unroll
         for (int c = 0; c < 16; ++c) out[c] = 0.0f;
-        if (jt + 1 < my_tiles) {
-          m0 = tile_m0(jt + 1);
-          n0 = tile_n0(jt + 1);
+        if (++it < n_items) {
+          t = item_lo(it);
+          hi = item_hi(it);
+          m0 = tile_m0(it);
+          n0 = tile_n0(it);
           row = m0 + q * 32 + lane;
         }
+      } else {
+        ++t;
       }
     }
     if (kPersist) {
@@ -426,13 +441,9 @@ cudaError_t launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const MvmAr
   const unsigned splits = SPLIT ? static_cast<unsigned>((a.Kt + a.tiles_per_split - 1) / a.tiles_per_split) : 1u;
   dim3 grid(static_cast<unsigned>((a.N + BN - 1) / BN), static_cast<unsigned>((a.M + kMvmBM - 1) / kMvmBM), splits);
   if (!SPLIT) {   // persistent: one CTA per SM (at most one fits, by shared memory)
-    static std::atomic<int> sm_count[128] = {};
-    int sms = sm_count[device].load(std::memory_order_relaxed);
-    if (sms == 0) {
-      e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-      if (e != cudaSuccess) return e;
-      sm_count[device].store(sms, std::memory_order_relaxed);
-    }
+    int sms = 0;
+    e = device_sm_count(device, &sms);
+    if (e != cudaSuccess) return e;
     const int64_t tiles = static_cast<int64_t>(grid.x) * grid.y;
     grid = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms), 1, 1);
   }
@@ -483,6 +494,30 @@ cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const MvmA
   }
 }
 
+// Tail reduction of a persistent launch: every element of the tail tiles is the sum, in K order, of
+// its tail_splits partials (tail_partial[tile * splits + s][row][col], tile-local), plus the bias.
+__global__ void tail_reduce_kernel(const float* __restrict__ tail_partial, int splits, int64_t dp_tiles,
+                                   int64_t tail_tiles, int bn, int64_t M, int64_t N, float* __restrict__ y,
+                                   int64_t rows_per_group, int64_t group_stride, int64_t row_stride,
+                                   int64_t col_stride, const float* __restrict__ bias) {
+  const int64_t per_tile = static_cast<int64_t>(kMvmBM) * bn;
+  const int64_t total = tail_tiles * per_tile;
+  const int64_t n_tiles_n = (N + bn - 1) / bn;
+  for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
+       e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t tl = e / per_tile, rem = e - tl * per_tile;
+    const int64_t r = rem / bn, c = rem - r * bn;
+    const int64_t tile = dp_tiles + tl;
+    const int64_t m = (tile / n_tiles_n) * kMvmBM + r, n = (tile % n_tiles_n) * bn + c;
+    if (m >= M || n >= N) continue;
+    float v = 0.0f;
+    for (int s = 0; s < splits; ++s) v += __ldg(tail_partial + (tl * splits + s) * per_tile + rem);
+    if (bias) v += __ldg(bias + n);
+    const int64_t grp = m / rows_per_group, rr = m - grp * rows_per_group;
+    y[grp * group_stride + rr * row_stride + n * col_stride] = v;
+  }
+}
+
 // Split-K reduction: y[layout(r, n)] = sum_s partial[s][r][n] + bias[n], splits added in order.
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int64_t M, int64_t N,
                                      float* __restrict__ y, int64_t rows_per_group, int64_t group_stride,
@@ -500,6 +535,31 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
 }
 
 }  // namespace
+
+cudaError_t device_sm_count(int device, int* sms) {
+  static std::atomic<int> sm_count[128] = {};
+  if (device < 0 || device >= 128) return cudaErrorInvalidDevice;
+  int v = sm_count[device].load(std::memory_order_relaxed);
+  if (v == 0) {
+    const cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return e;
+    sm_count[device].store(v, std::memory_order_relaxed);
+  }
+  *sms = v;
+  return cudaSuccess;
+}
+
+cudaError_t launch_tail_reduce(const float* tail_partial, int splits, int64_t dp_tiles, int64_t tail_tiles, int bn,
+                               int64_t M, int64_t N, float* y, int64_t rows_per_group, int64_t group_stride,
+                               int64_t row_stride, int64_t col_stride, const float* bias, cudaStream_t stream) {
+  const int64_t total = tail_tiles * kMvmBM * bn;
+  const int64_t blocks = (total + 255) / 256;
+  tail_reduce_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0, stream>>>(
+      tail_partial, splits, dp_tiles, tail_tiles, bn, M, N, y, rows_per_group, group_stride, row_stride, col_stride,
+      bias);
+  count_launch();
+  return cudaGetLastError();
+}
 
 cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, int64_t N, float* y,
                                  int64_t rows_per_group, int64_t group_stride, int64_t row_stride,

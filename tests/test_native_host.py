@@ -89,7 +89,8 @@ def test_split_k_workspace_choice():
     assert N.lib().mib_mvm_workspace(400, 600, xs, ws, kg, dev, f) == 0
     assert f.value > 0 and f.value % (400 * 600) == 0            # 52 output tiles: split the 16 K tiles
     assert N.lib().mib_mvm_workspace(16384, 3072, xs, ws, _kg(1024), dev, f) == 0
-    assert f.value == 0                                           # 8192 output tiles: no split
+    # 8192 output tiles: no split-K; their last wave of 52 tiles is cut into 2 K ranges
+    assert f.value == 52 * 2 * 128 * 48
 
 
 def test_split_k_balances_a_partly_idle_last_wave():
@@ -101,6 +102,19 @@ def test_split_k_balances_a_partly_idle_last_wave():
     assert f.value == 2 * 2048 * 1024
     assert N.lib().mib_mvm_workspace(4096, 1024, xs, ws, _kg(2048), dev, f) == 0
     assert f.value == 0                                           # 704 tiles: 4.76 waves, a split saves < 10%
+
+
+def test_tail_split_spreads_a_nearly_empty_last_wave():
+    """2816 output tiles (16384 x 1024 at 48 columns) take 20 waves of 148 SMs, the last holding 4 tiles:
+    the persistent launch steps 19 waves of whole tiles and cuts the 4 remaining ones into 16 ranges of
+    4 K tiles (one rescale group each), 64 partial tiles of 128 x 48 for the tail reduction.  A last wave
+    at least half full is not cut."""
+    xs, ws, dev = _spec(SM, (1, 32), (1, 128)), _spec(SM, (32, 32), (128, 128)), _dev(4096)
+    f = N.c_i64(-1)
+    assert N.lib().mib_mvm_workspace(16384, 1024, xs, ws, _kg(2048), dev, f) == 0
+    assert f.value == 4 * 16 * 128 * 48
+    assert N.lib().mib_mvm_workspace(16384, 6144, xs, ws, _kg(1024), dev, f) == 0
+    assert f.value == 0                                           # 16384 tiles: last wave 104 of 148
 
 
 def test_adc_plan_noisy_skips_table():
