@@ -12,9 +12,12 @@ input quant_gran (1,128) / paral (1,32), radc 4096, and the device model of
 the reference's Qwen3 example (HGS 1e-5, LGS 1e-8, 4 levels, rdac 4, read
 variation 0.05).  A step is one full prefill forward with loss.
 
-With N GPUs the headline layout is data parallel over the 8 sequences (every
-rank holds all crossbars, no collective on the data path but the loss mean);
-``--tp T`` shards every crossbar over groups of T ranks instead.  At N > 1 the
+With N GPUs the headline layout is data parallel over the 8 sequences: every
+rank holds all decoder-layer crossbars and a 1/N column shard of lm_head, so
+the only collectives are an all-gather of the final hidden states (8 MB per
+rank) and the loss's log-sum-exp all-reduces (``--no-head-shard``: a whole
+lm_head on every rank, no collective but the loss mean).  ``--tp T`` shards
+every crossbar over groups of T ranks instead.  At N > 1 the
 line also carries ``tp``: the same workload with every crossbar sharded over
 all N ranks (column-sharded q/k/v, gate/up and lm_head, row-sharded o and
 down), and ``layout_check``: the noise-free loss of both layouts, which must
@@ -380,7 +383,11 @@ def run_b200(args):
     # reference call) instead of independent replicas
     torch.manual_seed(1234)
     engine = DPETensor(device=dev, **ENGINE)
-    model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=tp_group)
+    # pure data parallelism: lm_head (a quarter of the crossbar cells) is still column-sharded over all
+    # ranks, which divides its programmed memory and per-call read-noise pass by the rank count
+    head_shard = world > 1 and tp == 1 and not args.no_head_shard
+    model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=tp_group,
+                            shard_head_over=dist.group.WORLD if head_shard else None)
     torch.cuda.synchronize()
     g = torch.Generator().manual_seed(1)
     ids_all = torch.randint(0, ARCH["vocab"], (BATCH, SEQ), generator=g).pin_memory()
@@ -423,7 +430,8 @@ def run_b200(args):
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "fp16",
                 "data": "synthetic",
-                "config": dict(base_config(), parallelism=f"dp{dp}xtp{tp}" if world > 1 else "single",
+                "config": dict(base_config(), parallelism=(f"dp{dp}xtp{tp}" + (f", lm_head column-sharded x{world}" if head_shard else ""))
+                                if world > 1 else "single",
                                l2="inputs larger than L2 (3 GB of programmed crossbars per forward)"),
                 "sliced_mvm_tops": ops_per_token() * tokens / (ms / 1000.0) / 1e12,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
@@ -463,6 +471,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp-compare", action="store_true",
                     help="at N > 1, skip the fully sharded layout's measurement and the layout check")
+    ap.add_argument("--no-head-shard", action="store_true",
+                    help="data parallel layout: keep a whole lm_head on every rank")
     ap.add_argument("--tp", type=int, default=0,
                     help="ranks per crossbar-sharding group (0: pure data parallel when the batch divides by the "
                          "rank count, else all ranks shard)")

@@ -6,8 +6,10 @@ along whole quantisation blocks, which keeps the result exact:
 
 * column sharding (``ColumnShardedLinearMem``): each rank programs a block of
   output columns (crossbar columns).  ADC, shift-add, block rescale and K-tile
-  sum are all per output column, so every shard's output is bit-identical to
-  the same columns of the unsharded layer.  The output stays sharded (the next
+  sum are all per output column, so every shard's output equals the same
+  columns of the unsharded layer: bit-identical, except where one of the two
+  launches sums an output tile's K ranges separately (split-K, or the tail
+  split of a persistent launch), which changes only the fp32 summation order.  The output stays sharded (the next
   layer consumes it sharded) or is all-gathered.
 * row sharding (``RowShardedLinearMem``): each rank programs a block of input
   rows (crossbar K tiles).  The K-tile partial sums are added after the ADC in
@@ -36,6 +38,17 @@ def shard_bounds(n: int, block: int, world: int, rank: int):
     b0 = rank * base + min(rank, extra)
     b1 = b0 + base + (1 if rank < extra else 0)
     return min(n, b0 * block), min(n, b1 * block)
+
+
+def noise_calls(world: int, rank: int, dim: int):
+    """(read-noise call, voltage-noise call) of a shard: the per-call noise kernels key their draws by
+    (seed, call, element), and every rank draws with the same seed.  Each rank's crossbar cells get a
+    draw of their own (call = rank), so shards are independent as the cells of one crossbar are; the
+    input of a column-sharded layer is replicated and keeps call 0 (one draw shared by all columns, as
+    in one crossbar), while a row shard's input features are its own (call = rank)."""
+    if world <= 1:
+        return 0, 0
+    return rank, (rank if dim == 1 else 0)
 
 
 def _world(group):
@@ -83,6 +96,11 @@ class _ShardBase(torch.nn.Module):
         self.in_features, self.out_features = in_f, out_f
         self.local = _LinearFromWeight(engine, w_local, b_local, input_slice, weight_slice, bw_e, input_paral_size,
                                        weight_paral_size, input_quant_gran, weight_quant_gran, device)
+        self._set_noise_calls(world, rank, dim)
+
+    def _set_noise_calls(self, world, rank, dim):
+        buf = self.local.weight_sliced._buf
+        buf["noise_call"], buf["input_noise_call"] = noise_calls(world, rank, dim)
 
     def prepare_for_inference(self):
         self.local.inference_mode = True
@@ -158,6 +176,7 @@ class ColumnShardedLinearMem(_ShardBase):
             fused = torch.cat(parts, dim=0)
             super().__init__(engine, fused, bias, 0, input_slice, weight_slice, presharded=True, **kw)
             self.group, self.world, self.rank = group, world, rank
+            self._set_noise_calls(world, rank, 0)
             self.gather = False
             self.shard_sizes = None
             return

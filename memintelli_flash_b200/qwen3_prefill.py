@@ -12,6 +12,14 @@ compactly so that its crossbars can be sharded across GPUs:
 * lm_head is column-sharded and the cross-entropy is computed without
   gathering the logits (distributed log-sum-exp).
 
+With ``shard_head_over`` the decoder layers stay whole on every rank (data
+parallel over sequences) and only lm_head is column-sharded over that group:
+the ranks' final hidden states are all-gathered, every rank computes its
+vocabulary columns for all sequences, and the distributed log-sum-exp gives
+every rank the loss of the whole batch.  lm_head holds about a quarter of the
+model's crossbar cells, so this divides its programmed memory and its per-call
+read-noise pass by the group size.
+
 With a world size of 1 there is no collective and no sharding.  Of the
 non-CIM parts, the RMSNorms and the SwiGLU run inside the input slicing, q/k
 RMSNorm + RoPE in one kernel (mib_qk_norm_rope_bf16), the loss's row
@@ -195,18 +203,27 @@ class Qwen3CimPrefill(torch.nn.Module):
     """Random-init Qwen3-architecture model; ``forward(ids)`` returns the mean next-token loss."""
 
     def __init__(self, engine, arch: Qwen3Arch = Qwen3Arch(), spec: CimSpec = CimSpec(), seed: int = 0,
-                 device=None, group=None, weights=None):
+                 device=None, group=None, weights=None, shard_head_over=None):
         """``weights``: optional state dict in Hugging Face Qwen3 naming (``model.embed_tokens.weight``,
         ``model.layers.{i}.self_attn.q_proj.weight``, ..., ``model.norm.weight``, ``lm_head.weight``), the
-        checkpoint the reference loads (memintelli/NN_models/Qwen3.py:136-140); random init otherwise."""
+        checkpoint the reference loads (memintelli/NN_models/Qwen3.py:136-140); random init otherwise.
+        ``group``: the ranks every crossbar is sharded over (None: all ranks).  ``shard_head_over``: a
+        group over which only lm_head is sharded, the layers being whole on each rank (``group`` must then
+        hold one rank); each rank's forward takes its own sequences and returns the loss of all of them."""
         super().__init__()
         device = device or engine.device
         self.arch, self.group, self.engine = arch, group, engine
         # sequences per forward are processed in this many groups when sharded, so that each group's
         # all-reduces overlap the other groups' crossbar work (see _layers_overlapped)
         self.micro_batches = 2
-        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        distributed = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if distributed else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
+        self.head_group = group if shard_head_over is None else shard_head_over
+        self.head_world = dist.get_world_size(self.head_group) if distributed else 1
+        self.head_gather = shard_head_over is not None and self.head_world > 1
+        if self.head_gather and self.world > 1:
+            raise ValueError("shard_head_over needs whole decoder layers on every rank (a group of one rank)")
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
         if weights is None:
@@ -223,7 +240,7 @@ class Qwen3CimPrefill(torch.nn.Module):
         w_head = torch.randn(arch.vocab, arch.hidden, generator=gen, device=device) * 0.02 if weights is None else \
             weights["lm_head.weight"].to(device=device, dtype=torch.float32)
         self.lm_head = ColumnShardedLinearMem(engine, w_head, None, spec.input_slice, spec.weight_slice,
-                                              group=group, device=device, **spec.kwargs())
+                                              group=self.head_group, device=device, **spec.kwargs())
         del w_head
         self._rope = {}
 
@@ -251,9 +268,19 @@ class Qwen3CimPrefill(torch.nn.Module):
             h = layer(h, cos, sin)
         return h
 
+    def _gather_head_inputs(self, h, ids):
+        """All ranks' final hidden states and ids, in rank order (lm_head sharded over data-parallel ranks)."""
+        if not self.head_gather:
+            return h, ids
+        hg = torch.empty((self.head_world * h.shape[0],) + tuple(h.shape[1:]), dtype=h.dtype, device=h.device)
+        dist.all_gather_into_tensor(hg, h.contiguous(), group=self.head_group)
+        ig = torch.empty((self.head_world * ids.shape[0],) + tuple(ids.shape[1:]), dtype=ids.dtype, device=ids.device)
+        dist.all_gather_into_tensor(ig, ids.contiguous(), group=self.head_group)
+        return hg, ig
+
     @torch.no_grad()
     def forward(self, ids: torch.Tensor) -> torch.Tensor:
-        h = self._hidden(ids)
+        h, ids = self._gather_head_inputs(self._hidden(ids), ids)
         xs = self.lm_head.new_input()
         self.engine.slice_rmsnorm_input(xs, h[:, :-1], self.norm, self.arch.eps)
         logits = self.lm_head.forward_sliced(xs)             # (B, T-1, V_local)
@@ -262,8 +289,9 @@ class Qwen3CimPrefill(torch.nn.Module):
 
     @torch.no_grad()
     def logits(self, ids: torch.Tensor) -> torch.Tensor:
-        """(B, T, V_local) logits of every position (this rank's vocabulary columns)."""
-        h = self._hidden(ids)
+        """(B, T, V_local) logits of every position (this rank's vocabulary columns; with
+        ``shard_head_over``, of every rank's sequences in rank order)."""
+        h, ids = self._gather_head_inputs(self._hidden(ids), ids)
         xs = self.lm_head.new_input()
         self.engine.slice_rmsnorm_input(xs, h, self.norm, self.arch.eps)
         return self.lm_head.forward_sliced(xs)
@@ -311,11 +339,11 @@ class Qwen3CimPrefill(torch.nn.Module):
         lmax, sexp, tgt = (torch.empty(rows, dtype=torch.float32, device=x.device) for _ in range(3))
         N.call("mib_row_logsumexp", N.ptr(x), rows, V, x.stride(0), N.ptr(tgt_ids), lo, N.ptr(lmax), N.ptr(sexp),
                N.ptr(tgt), N.stream_ptr(x.device))
-        if self.world > 1:
+        if self.head_world > 1:
             gmax = lmax.clone()
-            dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=self.group)
+            dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=self.head_group)
             sexp = sexp * torch.exp(lmax - gmax)
-            dist.all_reduce(sexp, group=self.group)
-            dist.all_reduce(tgt, group=self.group)
+            dist.all_reduce(sexp, group=self.head_group)
+            dist.all_reduce(tgt, group=self.head_group)
             lmax = gmax
         return (torch.log(sexp) + lmax - tgt).mean()

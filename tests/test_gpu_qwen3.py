@@ -40,6 +40,29 @@ def test_fused_columns_equal_separate_linears(cuda):
     assert np.linalg.norm(a - b) / np.linalg.norm(b) < 1e-6
 
 
+def test_shard_noise_calls_give_independent_draws(cuda):
+    """Every rank draws with the same seed; a crossbar shard's read variation is keyed by its own call
+    index (crossbar_shard.noise_calls), so two shards holding equal cells draw different noise, and the
+    same call index reproduces the same draw."""
+    import memintelli_flash_b200 as M
+    eng = M.DPETensor(device=cuda, **dict(NOISE_FREE, read_variation=0.05))
+    g = torch.Generator().manual_seed(5)
+    x, w = torch.randn(256, 512, generator=g), torch.randn(512, 384, generator=g) * 0.05
+    sm = torch.tensor([1, 1, 2, 2, 2])
+    xs = M.SlicedData(sm, is_weight=False, paral_size=(1, 32), quant_gran=(1, 128), device=cuda, inference=True)
+    ws = M.SlicedData(sm, is_weight=True, paral_size=(32, 32), quant_gran=(128, 128), device=cuda, inference=True)
+    xs.slice_data_imp(eng, x.to(cuda))
+    ws.slice_data_imp(eng, w.to(cuda))
+    ys = {}
+    for call in (0, 1, 0):
+        ws._buf["noise_call"] = call
+        torch.manual_seed(11)                  # one seed, as on every rank
+        ys.setdefault(call, []).append(eng(xs, ws).double().cpu().numpy())
+    assert np.array_equal(ys[0][0], ys[0][1])
+    d = np.linalg.norm(ys[0][0] - ys[1][0]) / np.linalg.norm(ys[0][0])
+    assert 1e-3 < d < 0.5                      # different draws of the same noise level
+
+
 def test_small_model_forward(cuda):
     import memintelli_flash_b200 as M
     from memintelli_flash_b200.qwen3_prefill import Qwen3Arch, Qwen3CimPrefill
@@ -76,19 +99,24 @@ def _shard_worker(rank, world, port, q):
     sharded = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=dev)
     loss_sharded = float(sharded(ids))
     dist.barrier()
+    solos = [dist.new_group([r]) for r in range(world)]     # every rank creates every group, in order
+    # decoder layers whole on each rank (one sequence each), lm_head sharded over both ranks
+    head_only = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=dev, group=solos[rank],
+                                shard_head_over=dist.group.WORLD)
+    loss_head = float(head_only(ids[rank:rank + 1]))
+    dist.barrier()
     if rank == 0:
-        solo = dist.new_group([0])
-    else:
-        dist.new_group([0])
-    if rank == 0:
-        single = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=dev, group=solo)
-        q.put((loss_sharded, float(single(ids))))
+        single = Qwen3CimPrefill(eng, Qwen3Arch(**SMALL), seed=1, device=dev, group=solos[0])
+        q.put((loss_sharded, loss_head, float(single(ids))))
     dist.barrier()
     dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_crossbar_sharded_model_matches_single_gpu():
+    """Two NCCL ranks, noise-free: every crossbar sharded over both ranks, and the decoder layers whole on
+    each rank (one sequence each) with only lm_head sharded.  Both losses equal the single-GPU loss of the
+    two sequences within 1e-5 (fp32 summation order of the row-sharded all-reduces)."""
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -101,7 +129,7 @@ def test_crossbar_sharded_model_matches_single_gpu():
     t0 = time.time()
     while True:                                   # fail fast if a rank dies
         try:
-            loss_sharded, loss_single = q.get(timeout=2)
+            loss_sharded, loss_head, loss_single = q.get(timeout=2)
             break
         except queue.Empty:
             dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
@@ -114,6 +142,7 @@ def test_crossbar_sharded_model_matches_single_gpu():
         p.join(timeout=120)
         assert p.exitcode == 0
     assert abs(loss_sharded - loss_single) < 1e-5 * abs(loss_single)
+    assert abs(loss_head - loss_single) < 1e-5 * abs(loss_single)
 
 
 def _small_reference_model(cuda, radc):

@@ -119,3 +119,13 @@ def test_sharding_rejects_string_granularity_and_empty_shards():
         assert got[r][1] and "string granularity" in got[r][1]
     assert len(got[0]) == 2
     assert got[1][2] and "empty crossbar shard" in got[1][2]
+
+
+def test_noise_calls_per_shard():
+    """Read variation: one call index per rank (shards draw independently, rank 0 keeps the unsharded
+    draw).  Voltage noise: row shards hold different input features (own call); column shards share the
+    replicated input (call 0, one draw for all columns as in one crossbar)."""
+    from memintelli_flash_b200.crossbar_shard import noise_calls
+    assert noise_calls(1, 0, 0) == (0, 0) and noise_calls(1, 0, 1) == (0, 0)
+    assert [noise_calls(4, r, 0) for r in range(4)] == [(0, 0), (1, 0), (2, 0), (3, 0)]
+    assert [noise_calls(4, r, 1) for r in range(4)] == [(0, 0), (1, 1), (2, 2), (3, 3)]
