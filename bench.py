@@ -388,6 +388,7 @@ def run_b200(args):
     head_shard = world > 1 and tp == 1 and not args.no_head_shard
     model = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=tp_group,
                             shard_head_over=dist.group.WORLD if head_shard else None)
+    model.prefetch_noise = args.noise_prefetch
     torch.cuda.synchronize()
     g = torch.Generator().manual_seed(1)
     ids_all = torch.randint(0, ARCH["vocab"], (BATCH, SEQ), generator=g).pin_memory()
@@ -398,6 +399,7 @@ def run_b200(args):
     tp_line = None
     if world > 1 and tp != world and not args.no_tp_compare:
         model_tp = Qwen3CimPrefill(engine, Qwen3Arch(**ARCH), seed=0, device=dev, group=None)
+        model_tp.prefetch_noise = args.noise_prefetch
         full = Layout(model_tp, ids_all, dev, world, world)
         rt = time_layout(full, engine, args, world, local, dev)
         # noise-free, both layouts compute the same losses up to fp32 summation order
@@ -471,6 +473,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp-compare", action="store_true",
                     help="at N > 1, skip the fully sharded layout's measurement and the layout check")
+    ap.add_argument("--noise-prefetch", action="store_true",
+                    help="run each layer's read-noise pass in the background of the layer before it "
+                         "(measured slower on B200)")
     ap.add_argument("--no-head-shard", action="store_true",
                     help="data parallel layout: keep a whole lm_head on every rank")
     ap.add_argument("--tp", type=int, default=0,

@@ -42,6 +42,10 @@ extern "C" {
 
 #define MIB_OPERAND_E4M3 0
 #define MIB_OPERAND_FP16 1
+/* FP16 input planes; weight planes as FP16 hi planes followed by FP16 lo planes ([2*S][N][Kt*pp], from
+ * mib_weight_read_noise_split): each crossbar MMA is followed by one on the lo planes into the same fp32
+ * accumulator, so non-integer conductances enter at 22 significand bits. */
+#define MIB_OPERAND_FP16_SPLIT 2
 
 #define MIB_MAX_SLICES 8
 #define MIB_MAX_LEVELS 256
@@ -166,6 +170,23 @@ int mib_input_noise(const uint8_t* planes_e4m3, __half* out_fp16, int64_t n_elem
  * present), else from the E4M3 level planes as level*Q_G + LGS. */
 int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16, int64_t n_elems,
                           const mib_device_spec* dev, uint64_t seed, uint64_t call, cudaStream_t stream);
+
+/* mib_weight_read_noise for the split weight operand (MIB_OPERAND_FP16_SPLIT): `out_fp16` holds
+ * 2 * n_elems halves, the FP16 rounding of every value followed by the FP16 rounding of its residual,
+ * so that hi + lo carries 22 significand bits.  Used for conductances with write variation, whose
+ * fixed-seed draw the reference evaluates in fp32 (memmat_tensor.py:175-180, 260-409).  n_elems must be
+ * a multiple of 8. */
+int mib_weight_read_noise_split(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16,
+                                int64_t n_elems, const mib_device_spec* dev, uint64_t seed, uint64_t call,
+                                cudaStream_t stream);
+
+/* mib_weight_read_noise (split != 0: mib_weight_read_noise_split) as a background pass: at most
+ * `max_blocks` blocks of 128 threads, each small enough to run on an SM beside a crossbar MVM CTA, so
+ * that a pass launched on a second stream ahead of its multiply overlaps the crossbar work running
+ * before it.  Same draws and outputs as the foreground entry points. */
+int mib_weight_read_noise_background(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16,
+                                     int64_t n_elems, const mib_device_spec* dev, uint64_t seed, uint64_t call,
+                                     int32_t split, int32_t max_blocks, cudaStream_t stream);
 
 /* ADC plan for one MVM configuration.  In the noise-free mode the ADC code
  * round_half_even(S * (radc_j - 1) / D) must be exact for every reachable

@@ -23,6 +23,7 @@ MIB_ERR_TIMEOUT = 5
 
 OPERAND_E4M3 = 0
 OPERAND_FP16 = 1
+OPERAND_FP16_SPLIT = 2     # FP16 inputs; weights as FP16 hi planes followed by FP16 lo planes
 
 MODE_LUT = 1
 MODE_FLOATACC = 2
@@ -67,6 +68,8 @@ _SIGS = {
                            c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp],
     "mib_input_noise": [c_vp, c_vp, c_i64, c_f64, c_u64, c_u64, c_vp],
     "mib_weight_read_noise": [c_vp, c_vp, c_vp, c_i64, _P(DeviceSpec), c_u64, c_u64, c_vp],
+    "mib_weight_read_noise_split": [c_vp, c_vp, c_vp, c_i64, _P(DeviceSpec), c_u64, c_u64, c_vp],
+    "mib_weight_read_noise_background": [c_vp, c_vp, c_vp, c_i64, _P(DeviceSpec), c_u64, c_u64, c_i32, c_i32, c_vp],
     "mib_adc_plan": [_P(SliceSpec), _P(SliceSpec), _P(KGeom), _P(DeviceSpec), _P(c_i32), _P(c_i32), c_vp],
     "mib_mvm": [c_vp, c_vp, c_i64, _P(SliceSpec), c_vp, c_vp, c_i64, _P(SliceSpec), _P(KGeom), _P(DeviceSpec), c_i32,
                 c_vp, c_i32, c_vp, _P(OutLayout), c_vp, c_vp, c_vp, c_i64, c_vp],

@@ -101,6 +101,8 @@ struct MvmArgs {
   float* tail_partial;
   int64_t wait_limit;       // cycles after which an abortable mbarrier wait gives up (about 2 s normally)
   int32_t hold_mma;         // test hook: the MMA warp issues nothing, so the epilogue's first wait runs out
+  int32_t b_split;          // 1: the weight planes are FP16 hi planes followed by lo planes ([2*Sy][N][K]);
+                            // every (K tile, input slice) MMA is followed by one on the lo planes
 };
 
 cudaError_t slice_dense(const float* x, int64_t ld_batch, int64_t ld_row, SliceArgs a, cudaStream_t stream);
@@ -113,8 +115,9 @@ cudaError_t slice_conv(const float* x, int64_t C, int64_t H, int64_t W, int64_t 
 cudaError_t program_weight(const float* w, int64_t stride_k, int64_t stride_n, ProgramArgs a, cudaStream_t stream);
 cudaError_t input_noise(const uint8_t* in, __half* out, int64_t n, float vnoise, uint64_t seed, uint64_t stream_id,
                         cudaStream_t stream);
-cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, int64_t n, ReadNoiseArgs a, uint64_t seed,
-                       uint64_t stream_id, cudaStream_t stream);
+cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, __half* out_lo, int64_t n,
+                       ReadNoiseArgs a, uint64_t seed, uint64_t stream_id, int background_blocks,
+                       cudaStream_t stream);
 void launch_block_exp(const float* bmax, float* bexp, int64_t n, cudaStream_t stream);
 cudaError_t qk_norm_rope(const float* qkv, int64_t tokens, int64_t ld_token, int seq_len, int q_heads, int kv_heads,
                          int head_dim, const float* q_norm, const float* k_norm, float eps, const float* cos_t,

@@ -651,10 +651,17 @@ int mib_input_noise(const uint8_t* planes_e4m3, __half* out_fp16, int64_t n_elem
   return MIB_OK;
 }
 
-int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16, int64_t n_elems,
-                          const mib_device_spec* dev, uint64_t seed, uint64_t call, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+int weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16, bool split,
+                      int64_t n_elems, const mib_device_spec* dev, uint64_t seed, uint64_t call,
+                      int background_blocks, cudaStream_t stream) {
+  if (background_blocks < 0) return fail(MIB_ERR_PARAM, "background block count must be >= 0");
   if ((!planes_e4m3 && !g_planes) || !out_fp16 || !dev) return fail(MIB_ERR_PARAM, "NULL argument");
   if (n_elems % 4) return fail(MIB_ERR_SHAPE, "element count must be a multiple of 4");
+  if (split && n_elems % 8) return fail(MIB_ERR_SHAPE, "element count must be a multiple of 8");
   mib::ReadNoiseArgs a;
   memset(&a, 0, sizeof(a));
   if (dev->g_level < 2 || !(dev->lgs < dev->hgs)) return fail(MIB_ERR_PARAM, "invalid conductance levels");
@@ -675,9 +682,33 @@ int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __h
   // memmat_tensor.py:218-233: identical sigmas skip the level lookup
   a.any_sigma = any ? 1 : 0;
   a.per_level = (any && !same) ? 1 : 0;
-  cudaError_t e = mib::read_noise(planes_e4m3, g_planes, out_fp16, n_elems, a, seed, (call << 2) | 2u, stream);
+  cudaError_t e = mib::read_noise(planes_e4m3, g_planes, out_fp16, split ? out_fp16 + n_elems : nullptr, n_elems, a,
+                                  seed, (call << 2) | 2u, background_blocks, stream);
   if (e != cudaSuccess) return cuda_fail(e, "read_noise launch");
   return MIB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mib_weight_read_noise(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16, int64_t n_elems,
+                          const mib_device_spec* dev, uint64_t seed, uint64_t call, cudaStream_t stream) {
+  return weight_read_noise(planes_e4m3, g_planes, out_fp16, false, n_elems, dev, seed, call, 0, stream);
+}
+
+int mib_weight_read_noise_split(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16,
+                                int64_t n_elems, const mib_device_spec* dev, uint64_t seed, uint64_t call,
+                                cudaStream_t stream) {
+  return weight_read_noise(planes_e4m3, g_planes, out_fp16, true, n_elems, dev, seed, call, 0, stream);
+}
+
+int mib_weight_read_noise_background(const uint8_t* planes_e4m3, const float* g_planes, __half* out_fp16,
+                                     int64_t n_elems, const mib_device_spec* dev, uint64_t seed, uint64_t call,
+                                     int32_t split, int32_t max_blocks, cudaStream_t stream) {
+  if (max_blocks < 1) return fail(MIB_ERR_PARAM, "max_blocks must be positive");
+  return weight_read_noise(planes_e4m3, g_planes, out_fp16, split != 0, n_elems, dev, seed, call, max_blocks,
+                           stream);
 }
 
 int mib_adc_plan(const mib_slice_spec* x_spec, const mib_slice_spec* w_spec, const mib_k_geom* kg,
@@ -733,9 +764,11 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   if (int r = make_tab(w_spec, tw)) return r;
   if (!a_planes || !a_scale || !b_planes || !b_scale || !y || !layout || !dev)
     return fail(MIB_ERR_PARAM, "NULL argument");
-  if (operand_kind != MIB_OPERAND_E4M3 && operand_kind != MIB_OPERAND_FP16)
+  if (operand_kind != MIB_OPERAND_E4M3 && operand_kind != MIB_OPERAND_FP16 && operand_kind != MIB_OPERAND_FP16_SPLIT)
     return fail(MIB_ERR_PARAM, "unknown operand kind");
-  if (int r = check_kgeom(kg, operand_kind)) return r;
+  const bool b_split = operand_kind == MIB_OPERAND_FP16_SPLIT;
+  const int kind = b_split ? MIB_OPERAND_FP16 : operand_kind;   // element type of both operands' planes
+  if (int r = check_kgeom(kg, kind)) return r;
   if (m < 1 || n < 1) return fail(MIB_ERR_SHAPE, "empty matmul");
   if (m > 65535LL * mib::kMvmBM) return fail(MIB_ERR_UNSUPPORTED, "too many rows for one launch");
   if (x_spec->paral[1] != kg->p || w_spec->paral[0] != kg->p)
@@ -764,11 +797,13 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   a.pp = kg->pp;
   a.Sx = tx.S;
   a.Sy = tw.S;
-  a.row_bytes = kg->pp * esize(operand_kind);
+  a.row_bytes = kg->pp * esize(kind);
   const int bn = 16 * mib::mvm_column_groups(tw.S);
+  const int b_planes_n = b_split ? 2 * tw.S : tw.S;
   a.a_slice_bytes = static_cast<uint32_t>(mib::kMvmBM * a.row_bytes);
   a.b_slice_bytes = static_cast<uint32_t>(bn * a.row_bytes);
-  a.stage_bytes = static_cast<uint32_t>(tx.S) * a.a_slice_bytes + static_cast<uint32_t>(tw.S) * a.b_slice_bytes;
+  a.stage_bytes = static_cast<uint32_t>(tx.S) * a.a_slice_bytes + static_cast<uint32_t>(b_planes_n) * a.b_slice_bytes;
+  a.b_split = b_split ? 1 : 0;
   a.lut_len = pl.lut_len;
   a.lut = adc_table;
   a.lut_smem = (pl.mode & mib::MODE_LUT) && static_cast<size_t>(tw.S) * pl.lut_len * 4 <= 48 * 1024 ? 1 : 0;
@@ -821,9 +856,9 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
     g_inject_wait_limit = 0;
   }
   CUtensorMap ta, tb;
-  if (int r = encode_planes(&ta, a_planes, operand_kind, m, kg->kt * kg->pp, tx.S, kg->pp, mib::kMvmBM)) return r;
-  if (int r = encode_planes(&tb, b_planes, operand_kind, n, kg->kt * kg->pp, tw.S, kg->pp, bn)) return r;
-  cudaError_t e = mib::launch_mvm(ta, tb, a, operand_kind, mode, stream);
+  if (int r = encode_planes(&ta, a_planes, kind, m, kg->kt * kg->pp, tx.S, kg->pp, mib::kMvmBM)) return r;
+  if (int r = encode_planes(&tb, b_planes, kind, n, kg->kt * kg->pp, b_planes_n, kg->pp, bn)) return r;
+  cudaError_t e = mib::launch_mvm(ta, tb, a, kind, mode, stream);
   if (e != cudaSuccess) return cuda_fail(e, "mvm launch");
   if (a.partial) {
     e = mib::launch_splitk_reduce(a.partial, sp.splits, m, n, y, a.rows_per_group, a.group_stride, a.row_stride,

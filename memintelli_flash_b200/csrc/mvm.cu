@@ -35,6 +35,21 @@ constexpr int kSlotCols = 256;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer (half-even)
 constexpr uint32_t kMagicBits = 0x4B400000u;
 
+// Order in which a persistent launch steps through the output tiles: bands of kTileBandRows row tiles,
+// each band column by column (row tiles fastest).  The SMs then work on one band's rows at a time and
+// every weight column tile is read from DRAM once per band, not once per row tile: for a 1024 x 151936
+// lm_head at 16384 rows that is 8 passes over the weights instead of 128.
+constexpr int64_t kTileBandRows = 16;
+__host__ __device__ __forceinline__ void tile_coords(int64_t idx, int64_t n_tiles_m, int64_t n_tiles_n,
+                                                     int64_t* tm, int64_t* tn) {
+  const int64_t band = idx / (kTileBandRows * n_tiles_n);
+  const int64_t first = band * kTileBandRows;
+  const int64_t rows = n_tiles_m - first < kTileBandRows ? n_tiles_m - first : kTileBandRows;
+  const int64_t local = idx - band * kTileBandRows * n_tiles_n;
+  *tm = first + local % rows;
+  *tn = local / rows;
+}
+
 struct SmemCtl {
   uint64_t full[8];
   uint64_t empty[8];
@@ -101,13 +116,14 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   int32_t* lut_s = reinterpret_cast<int32_t*>(ctl + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Persistent (launches without split-K): CTA b processes output tiles b, b + grid, ... (column tiles
-  // fastest).  The stage ring, the TMEM slots and the barrier phases run on across tiles, so the next
+  // Persistent (launches without split-K): CTA b processes output tiles b, b + grid, ... in the order of
+  // tile_coords.  The stage ring, the TMEM slots and the barrier phases run on across tiles, so the next
   // tile's loads and MMAs proceed while this tile's outputs are stored.  The CTA's work is a list of
   // items: its whole tiles below dp_tiles, then at most one K range of a tail tile (see MvmArgs).
   constexpr bool kPersist = !SPLIT;
   const int64_t n_tiles_n = (P.N + BN - 1) / BN;
-  const int64_t n_tiles = n_tiles_n * ((P.M + kMvmBM - 1) / kMvmBM);
+  const int64_t n_tiles_m = (P.M + kMvmBM - 1) / kMvmBM;
+  const int64_t n_tiles = n_tiles_n * n_tiles_m;
   const int64_t bx = blockIdx.x;
   const int64_t my_dp = kPersist ? (P.dp_tiles > bx ? (P.dp_tiles - bx + gridDim.x - 1) / gridDim.x : 0) : 1;
   const int tail_s = kPersist ? P.tail_splits : 0;
@@ -115,13 +131,19 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   const int n_items_tail = has_tail ? 1 : 0;
   const int64_t n_items = my_dp + n_items_tail;
   auto item_tile = [&](int64_t it) -> int64_t {   // linear output tile of item `it` (persistent)
-    return it < my_dp ? bx + it * gridDim.x : P.dp_tiles + bx / tail_s;
+    return it < my_dp ? bx + it * gridDim.x : P.dp_tiles + bx / (tail_s > 0 ? tail_s : 1);
   };
   auto tile_m0 = [&](int64_t it) -> int64_t {
-    return kPersist ? (item_tile(it) / n_tiles_n) * kMvmBM : static_cast<int64_t>(blockIdx.y) * kMvmBM;
+    if (!kPersist) return static_cast<int64_t>(blockIdx.y) * kMvmBM;
+    int64_t tm, tn;
+    tile_coords(item_tile(it), n_tiles_m, n_tiles_n, &tm, &tn);
+    return tm * kMvmBM;
   };
   auto tile_n0 = [&](int64_t it) -> int64_t {
-    return kPersist ? (item_tile(it) % n_tiles_n) * BN : static_cast<int64_t>(blockIdx.x) * BN;
+    if (!kPersist) return static_cast<int64_t>(blockIdx.x) * BN;
+    int64_t tm, tn;
+    tile_coords(item_tile(it), n_tiles_m, n_tiles_n, &tm, &tn);
+    return tn * BN;
   };
   constexpr int Sy = SY;
   const int Sx = SXC > 0 ? SXC : P.Sx;
@@ -226,6 +248,14 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
             const uint64_t ad = smem_desc(a_base + i * P.a_slice_bytes + kk * 32, P.row_bytes);
             const uint64_t bd = smem_desc(b_base + kk * 32, P.row_bytes);
             tc_mma<KIND>(d, ad, bd, idesc, kk > 0 ? 1u : 0u);
+          }
+          if (P.b_split) {   // the FP16 residuals of the weight planes, into the same accumulator
+            const uint32_t b_lo = b_base + static_cast<uint32_t>(Sy) * P.b_slice_bytes;
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const uint64_t ad = smem_desc(a_base + i * P.a_slice_bytes + kk * 32, P.row_bytes);
+              const uint64_t bd = smem_desc(b_lo + kk * 32, P.row_bytes);
+              tc_mma<KIND>(d, ad, bd, idesc, 1u);
+            }
           }
           tc_commit(&ctl->tfull[slot]);
           ++uses;
@@ -502,13 +532,14 @@ __global__ void tail_reduce_kernel(const float* __restrict__ tail_partial, int s
                                    int64_t col_stride, const float* __restrict__ bias) {
   const int64_t per_tile = static_cast<int64_t>(kMvmBM) * bn;
   const int64_t total = tail_tiles * per_tile;
-  const int64_t n_tiles_n = (N + bn - 1) / bn;
+  const int64_t n_tiles_n = (N + bn - 1) / bn, n_tiles_m = (M + kMvmBM - 1) / kMvmBM;
   for (int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; e < total;
        e += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int64_t tl = e / per_tile, rem = e - tl * per_tile;
     const int64_t r = rem / bn, c = rem - r * bn;
-    const int64_t tile = dp_tiles + tl;
-    const int64_t m = (tile / n_tiles_n) * kMvmBM + r, n = (tile % n_tiles_n) * bn + c;
+    int64_t tm, tn;
+    tile_coords(dp_tiles + tl, n_tiles_m, n_tiles_n, &tm, &tn);
+    const int64_t m = tm * kMvmBM + r, n = tn * bn + c;
     if (m >= M || n >= N) continue;
     float v = 0.0f;
     for (int s = 0; s < splits; ++s) v += __ldg(tail_partial + (tl * splits + s) * per_tile + rem);

@@ -617,11 +617,11 @@ __global__ void input_noise_kernel(const uint8_t* __restrict__ in, __half* __res
 // (G = L Q_G + LGS) the output is L e + (LGS / Q_G)(e - 1) with e = exp(sigma z): no division, and L
 // itself indexes a per-level sigma (the reference recovers it as round((G - LGS) / Q_G)).  Conductance
 // planes (write variation present) go through G directly.
-__device__ __forceinline__ uint2 read_noise_group(uint32_t lv_raw, const float* __restrict__ gp, int64_t grp,
-                                                  const ReadNoiseArgs& a, uint64_t seed, uint64_t stream) {
+__device__ __forceinline__ void read_noise_group(uint32_t lv_raw, const float* __restrict__ gp, int64_t grp,
+                                                 const ReadNoiseArgs& a, uint64_t seed, uint64_t stream,
+                                                 float (&o)[4]) {
   float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   if (a.any_sigma) normal4(seed, stream, static_cast<uint64_t>(grp), z);
-  float o[4];
   if (gp) {
     const float4 g4 = reinterpret_cast<const float4*>(gp)[grp];
     const float g[4] = {g4.x, g4.y, g4.z, g4.w};
@@ -651,39 +651,60 @@ __device__ __forceinline__ uint2 read_noise_group(uint32_t lv_raw, const float* 
       }
     }
   }
+}
+
+// FP16 of 4 values, and (lo) of what that rounding left out: hi + lo carries 22 significand bits.
+__device__ __forceinline__ uint2 half4_hi(const float (&o)[4]) {
   const __half2 h0 = __floats2half2_rn(o[0], o[1]), h1 = __floats2half2_rn(o[2], o[3]);
-  uint2 r;
-  r.x = *reinterpret_cast<const uint32_t*>(&h0);
-  r.y = *reinterpret_cast<const uint32_t*>(&h1);
-  return r;
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+}
+__device__ __forceinline__ uint2 half4_lo(const float (&o)[4], uint2 hi) {
+  const __half2 h0 = *reinterpret_cast<const __half2*>(&hi.x), h1 = *reinterpret_cast<const __half2*>(&hi.y);
+  const __half2 l0 = __floats2half2_rn(o[0] - __low2float(h0), o[1] - __high2float(h0));
+  const __half2 l1 = __floats2half2_rn(o[2] - __low2float(h1), o[3] - __high2float(h1));
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
 }
 
 // Two 4-cell groups per thread (8 B of levels in, 16 B of FP16 out) when the buffers allow the wide
 // accesses, else one group per thread.  Group g always draws Philox block g, so both forms give the
 // same values.
+// With out_lo (the weight operand split into FP16 hi and lo planes), the residual of every value's FP16
+// rounding goes to out_lo at the same index.
 template <bool WIDE>
 __global__ void read_noise_kernel(const uint8_t* __restrict__ levels, const float* __restrict__ gp,
-                                  __half* __restrict__ out, int64_t n4, ReadNoiseArgs a, uint64_t seed,
-                                  uint64_t stream) {
+                                  __half* __restrict__ out, __half* __restrict__ out_lo, int64_t n4, ReadNoiseArgs a,
+                                  uint64_t seed, uint64_t stream) {
   const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  float o0[4], o1[4];
   if constexpr (WIDE) {
     const int64_t n8 = n4 / 2;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8; i += step) {
       uint2 raw = make_uint2(0u, 0u);
       if (!gp) raw = reinterpret_cast<const uint2*>(levels)[i];
-      const uint2 o0 = read_noise_group(raw.x, gp, 2 * i, a, seed, stream);
-      const uint2 o1 = read_noise_group(raw.y, gp, 2 * i + 1, a, seed, stream);
-      reinterpret_cast<uint4*>(out)[i] = make_uint4(o0.x, o0.y, o1.x, o1.y);
+      read_noise_group(raw.x, gp, 2 * i, a, seed, stream, o0);
+      read_noise_group(raw.y, gp, 2 * i + 1, a, seed, stream, o1);
+      const uint2 h0 = half4_hi(o0), h1 = half4_hi(o1);
+      reinterpret_cast<uint4*>(out)[i] = make_uint4(h0.x, h0.y, h1.x, h1.y);
+      if (out_lo) {
+        const uint2 l0 = half4_lo(o0, h0), l1 = half4_lo(o1, h1);
+        reinterpret_cast<uint4*>(out_lo)[i] = make_uint4(l0.x, l0.y, l1.x, l1.y);
+      }
     }
     if ((n4 & 1) && blockIdx.x == 0 && threadIdx.x == 0) {
       const int64_t g = n4 - 1;
       const uint32_t raw = gp ? 0u : reinterpret_cast<const uint32_t*>(levels)[g];
-      reinterpret_cast<uint2*>(out)[g] = read_noise_group(raw, gp, g, a, seed, stream);
+      read_noise_group(raw, gp, g, a, seed, stream, o0);
+      const uint2 h0 = half4_hi(o0);
+      reinterpret_cast<uint2*>(out)[g] = h0;
+      if (out_lo) reinterpret_cast<uint2*>(out_lo)[g] = half4_lo(o0, h0);
     }
   } else {
     for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < n4; g += step) {
       const uint32_t raw = gp ? 0u : reinterpret_cast<const uint32_t*>(levels)[g];
-      reinterpret_cast<uint2*>(out)[g] = read_noise_group(raw, gp, g, a, seed, stream);
+      read_noise_group(raw, gp, g, a, seed, stream, o0);
+      const uint2 h0 = half4_hi(o0);
+      reinterpret_cast<uint2*>(out)[g] = h0;
+      if (out_lo) reinterpret_cast<uint2*>(out_lo)[g] = half4_lo(o0, h0);
     }
   }
 }
@@ -854,15 +875,23 @@ cudaError_t input_noise(const uint8_t* in, __half* out, int64_t n, float vnoise,
   return cudaGetLastError();
 }
 
-cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, int64_t n, ReadNoiseArgs a, uint64_t seed,
-                       uint64_t stream_id, cudaStream_t stream) {
+cudaError_t read_noise(const uint8_t* levels, const float* gp, __half* out, __half* out_lo, int64_t n,
+                       ReadNoiseArgs a, uint64_t seed, uint64_t stream_id, int background_blocks,
+                       cudaStream_t stream) {
   const int64_t n4 = n / 4;
   const bool wide = (reinterpret_cast<uintptr_t>(levels) % 8 == 0) && (reinterpret_cast<uintptr_t>(gp) % 32 == 0) &&
-                    (reinterpret_cast<uintptr_t>(out) % 16 == 0);
+                    (reinterpret_cast<uintptr_t>(out) % 16 == 0) && (reinterpret_cast<uintptr_t>(out_lo) % 16 == 0);
+  // background: at most `background_blocks` blocks of 128 threads stepping through the cells, small
+  // enough (4 warps, at most 64 registers a thread, no shared memory) to run beside a crossbar MVM CTA
+  const int threads = background_blocks > 0 ? 128 : 256;
+  auto grid = [&](int64_t items) {
+    const int g = grid_for(items, threads);
+    return background_blocks > 0 && g > background_blocks ? background_blocks : g;
+  };
   if (wide)
-    read_noise_kernel<true><<<grid_for(n4 / 2 + 1, 256), 256, 0, stream>>>(levels, gp, out, n4, a, seed, stream_id);
+    read_noise_kernel<true><<<grid(n4 / 2 + 1), threads, 0, stream>>>(levels, gp, out, out_lo, n4, a, seed, stream_id);
   else
-    read_noise_kernel<false><<<grid_for(n4, 256), 256, 0, stream>>>(levels, gp, out, n4, a, seed, stream_id);
+    read_noise_kernel<false><<<grid(n4), threads, 0, stream>>>(levels, gp, out, out_lo, n4, a, seed, stream_id);
   count_launch();
   return cudaGetLastError();
 }

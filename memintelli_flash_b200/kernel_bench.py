@@ -28,9 +28,12 @@ from .pimpy import DPETensor, SlicedData
 SLICES = [1, 1, 2, 2, 2]
 
 
-def _engine(device, noisy):
+def _engine(device, noisy, read_only=False):
+    """noisy: read variation and voltage noise 0.05; read_only: read variation 0.05 alone (the device model
+    of the Qwen3 prefill bench, whose inputs are sliced straight into FP16 planes)."""
     return DPETensor(HGS=1e-5, LGS=1e-8, write_variation=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0,
-                     read_variation=0.05 if noisy else 0.0, vnoise=0.05 if noisy else 0.0,
+                     read_variation=0.05 if (noisy or read_only) else 0.0,
+                     vnoise=0.05 if (noisy and not read_only) else 0.0,
                      rdac=4, g_level=4, radc=4096, device=device)
 
 
@@ -72,9 +75,9 @@ def bench_slice(rows, cols, bfp=False, iters=20, device="cuda:0", fp16=False):
     return us
 
 
-def bench_mvm(m, k, n, noisy=False, bfp=False, iters=10, device="cuda:0"):
+def bench_mvm(m, k, n, noisy=False, bfp=False, iters=10, device="cuda:0", read_only=False):
     dev = torch.device(device)
-    eng = _engine(dev, noisy)
+    eng = _engine(dev, noisy, read_only)
     x = torch.randn(m, k, device=dev)
     w = torch.randn(k, n, device=dev)
     xs, ws = _input(dev, bfp), _weight(dev, bfp)
@@ -91,7 +94,8 @@ def bench_mvm(m, k, n, noisy=False, bfp=False, iters=10, device="cuda:0"):
     log, eng.launch_log = eng.launch_log, None
     ms = sorted(a.elapsed_time(b) for a, b, _, _ in log)[len(log) // 2]
     ops, adc = log[0][2], log[0][3]
-    print(f"mvm m={m} k={k} n={n} noisy={noisy} bfp={bfp}: {ms:.3f} ms, {ops / ms / 1e9:.1f} slice-pair TOPS, "
+    print(f"mvm m={m} k={k} n={n} noisy={noisy} read_only={read_only} bfp={bfp}: {ms:.3f} ms, "
+          f"{ops / ms / 1e9:.1f} slice-pair TOPS, "
           f"{adc / ms / 1e9:.3f} T ADC events/s", flush=True)
     return ms
 
@@ -295,6 +299,8 @@ def main(argv=None):
     v.add_argument("--k", type=int, default=4096)
     v.add_argument("--n", type=int, default=4096)
     v.add_argument("--noisy", action="store_true")
+    v.add_argument("--read-noise-only", action="store_true",
+                   help="read variation 0.05 without voltage noise, as in the Qwen3 prefill bench")
     v.add_argument("--bfp", action="store_true")
     v.add_argument("--iters", type=int, default=10)
     z = sub.add_parser("noise")
@@ -309,7 +315,7 @@ def main(argv=None):
     if a.kernel == "slice":
         bench_slice(a.rows, a.cols, a.bfp, a.iters, fp16=a.fp16)
     elif a.kernel == "mvm":
-        bench_mvm(a.m, a.k, a.n, a.noisy, a.bfp, a.iters)
+        bench_mvm(a.m, a.k, a.n, a.noisy, a.bfp, a.iters, read_only=a.read_noise_only)
     elif a.kernel == "noise":
         bench_noise(a.k, a.n, a.iters, a.per_level)
     else:

@@ -365,6 +365,61 @@ class DPETensor(object):
             self._plans[key] = (mode.value, table, n.value)
         return self._plans[key]
 
+    def _weight_read_noise(self, mat: SlicedData, dspec, seed: int, dev, stream, background_blocks: int):
+        """FP16 weight planes of one multiply (read variation drawn with ``seed``) and their operand kind.
+        A crossbar shard draws its cells' read variation on a call index of its own
+        (crossbar_shard.noise_calls); an unsharded crossbar uses call 0.  Conductances with write
+        variation (a fixed-seed draw the reference evaluates in fp32) become FP16 hi and lo planes,
+        multiplied into one accumulator (22 significand bits)."""
+        b_planes, g_planes = mat._buf["planes"], mat._buf.get("g_planes")
+        split = g_planes is not None
+        shape = ((2 if split else 1) * b_planes.shape[0],) + tuple(b_planes.shape[1:])
+        b16 = torch.empty(shape, dtype=torch.float16, device=dev)
+        call = mat._buf.get("noise_call", 0)
+        if background_blocks:
+            N.call("mib_weight_read_noise_background", N.ptr(b_planes), N.ptr(g_planes), N.ptr(b16),
+                   b_planes.numel(), dspec, seed, call, int(split), background_blocks, stream)
+        elif split:
+            N.call("mib_weight_read_noise_split", N.ptr(b_planes), N.ptr(g_planes), N.ptr(b16), b_planes.numel(),
+                   dspec, seed, call, stream)
+        else:
+            N.call("mib_weight_read_noise", N.ptr(b_planes), None, N.ptr(b16), b_planes.numel(), dspec, seed, call,
+                   stream)
+        return b16, (N.OPERAND_FP16_SPLIT if split else N.OPERAND_FP16)
+
+    def draw_read_noise(self, mat: SlicedData, uses: int = 1, background: bool = True):
+        """Draw the read variation of ``mat``'s next ``uses`` multiplies now: they share this one draw (and
+        its seed) instead of each running the pass, as the sequences of one reference call share one
+        draw.  ``background``: the pass runs on a side stream with one small block per SM, beside the
+        crossbar work already queued, and the first multiply waits for it; otherwise it runs on the
+        current stream at full width.  The seed is taken from torch's generator here, so a program that
+        draws in a fixed order is reproducible under ``torch.manual_seed`` (with other draws than the
+        same program drawing at each multiply).  No effect on a noise-free engine or an unprogrammed
+        weight."""
+        if not self.noisy or mat._buf is None or not mat.is_weight or mat._buf.get("views_only"):
+            return
+        if mat._buf["kind"] != N.OPERAND_E4M3 or uses < 1:
+            return
+        dev = mat._buf["planes"].device
+        dspec = self._device_spec()
+        seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+        if background:
+            streams = self.__dict__.setdefault("_noise_streams", {})
+            if dev.index not in streams:
+                streams[dev.index] = (torch.cuda.Stream(device=dev),
+                                      torch.cuda.get_device_properties(dev).multi_processor_count)
+            side, sms = streams[dev.index]
+            with torch.cuda.stream(side):
+                b16, kind = self._weight_read_noise(mat, dspec, seed, dev, N.stream_ptr(dev), sms)
+                ready = torch.cuda.Event()
+                ready.record(side)
+        else:
+            b16, kind = self._weight_read_noise(mat, dspec, seed, dev, N.stream_ptr(dev), 0)
+            ready = torch.cuda.Event()
+            ready.record()
+        mat._buf["prefetched_noise"] = dict(planes=b16, kind=kind, seed=seed, ready=ready, dspec=bytes(dspec),
+                                            uses=uses)
+
     def _mvm(self, x: SlicedData, mat: SlicedData, out=None, bias=None, layout=None, acc_dump=None):
         if x._buf is None or mat._buf is None:
             raise ValueError('slice_data_imp must be called on both operands first')
@@ -392,12 +447,21 @@ class DPETensor(object):
             if kind != N.OPERAND_E4M3:
                 raise NotImplementedError('noisy crossbars with more than 16 DAC / conductance levels')
             fused_seed = x._buf.get("noise_seed")
+            pre = mat._buf.get("prefetched_noise")
+            if pre is not None:
+                pre["uses"] -= 1
+                if pre["uses"] <= 0:
+                    del mat._buf["prefetched_noise"]
+                if fused_seed is not None or pre["dspec"] != bytes(dspec):
+                    pre = None                 # drawn for another seed source or device model: draw again
             if fused_seed is not None:
                 # sliced with this multiply's voltage noise already applied (conv input, sliced per multiply)
                 if x._buf.get("noise_used") or x._buf.get("vnoise") != float(self.vnoise):
                     raise ValueError('this sliced input carries the voltage noise of one multiply; slice it again')
                 x._buf["noise_used"] = True
                 seed = fused_seed
+            elif pre is not None:
+                seed = pre["seed"]
             else:
                 seed = int(torch.randint(0, 2 ** 62, (1,)).item())
             if fused_seed is not None:
@@ -410,11 +474,15 @@ class DPETensor(object):
             else:
                 a16 = torch.empty(a_planes.shape, dtype=torch.float16, device=dev)
                 N.call("mib_input_noise", N.ptr(a_planes), N.ptr(a16), a_planes.numel(), float(self.vnoise), seed,
-                       0, stream)
-            b16 = torch.empty(b_planes.shape, dtype=torch.float16, device=dev)
-            N.call("mib_weight_read_noise", N.ptr(b_planes), N.ptr(mat._buf.get("g_planes")), N.ptr(b16),
-                   b_planes.numel(), dspec, seed, 0, stream)
-            a_planes, b_planes, kind = a16, b16, N.OPERAND_FP16
+                       mat._buf.get("input_noise_call", 0), stream)
+            if pre is not None:
+                main = torch.cuda.current_stream(dev)
+                main.wait_event(pre["ready"])
+                b16, kind = pre["planes"], pre["kind"]
+                b16.record_stream(main)        # allocated on the side stream, read on this one
+            else:
+                b16, kind = self._weight_read_noise(mat, dspec, seed, dev, stream, 0)
+            a_planes, b_planes = a16, b16
         mode, table, tlen = self._plan(xs, ws, kg, dspec, dev)
         wkey = (M, Nc, bytes(xs), bytes(ws), bytes(kg), bytes(dspec))
         if wkey not in self._ws_floats:

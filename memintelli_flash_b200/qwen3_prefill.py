@@ -216,6 +216,11 @@ class Qwen3CimPrefill(torch.nn.Module):
         # sequences per forward are processed in this many groups when sharded, so that each group's
         # all-reduces overlap the other groups' crossbar work (see _layers_overlapped)
         self.micro_batches = 2
+        # True: read-noise pass of layer i + 1 (of lm_head after the last layer) launched as a background pass
+        # on a side stream while layer i runs (DPETensor.draw_read_noise).  Off: on one B200 the background
+        # blocks took more from the crossbar kernel beside them than the pass costs in front of its multiply
+        # (one 2048-token rank's forward 128.3 -> 146.4 ms; the 8 x 2048 bench 17.49 k -> 17.23 k tokens/s).
+        self.prefetch_noise = False
         distributed = dist.is_available() and dist.is_initialized()
         self.world = dist.get_world_size(group) if distributed else 1
         self.rank = dist.get_rank(group) if self.world > 1 else 0
@@ -255,6 +260,17 @@ class Qwen3CimPrefill(torch.nn.Module):
         for layer in self.layers:
             layer.attn_dtype = dtype
 
+    def _draw_noise(self, layer_or_head, uses, background):
+        """One read-variation draw for each crossbar array of a layer (or lm_head), shared by its next
+        ``uses`` multiplies (DPETensor.draw_read_noise)."""
+        if layer_or_head is self.lm_head:
+            arrays = [self.lm_head]
+        else:
+            arrays = [layer_or_head.qkv_proj, layer_or_head.o_proj, layer_or_head.gate_up_proj,
+                      layer_or_head.down_proj]
+        for arr in arrays:
+            self.engine.draw_read_noise(arr.local.weight_sliced, uses=uses, background=background)
+
     def _hidden(self, ids):
         a = self.arch
         B, T = ids.shape
@@ -264,7 +280,11 @@ class Qwen3CimPrefill(torch.nn.Module):
         h = F.embedding(ids, self.embed)
         if self.world > 1 and self.micro_batches > 1 and B >= self.micro_batches:
             return self._layers_overlapped(h, cos, sin)
-        for layer in self.layers:
+        layers = list(self.layers)
+        for i, layer in enumerate(layers):
+            if self.prefetch_noise:
+                # the next layer's (or lm_head's) read-noise pass runs in the background of this layer
+                self._draw_noise(layers[i + 1] if i + 1 < len(layers) else self.lm_head, 1, True)
             h = layer(h, cos, sin)
         return h
 
@@ -314,7 +334,16 @@ class Qwen3CimPrefill(torch.nn.Module):
         def launch(m, y):
             pending[m] = (y, dist.all_reduce(y, group=self.group, async_op=True))
 
-        for layer in self.layers:
+        # every array is multiplied once per group: one read-variation draw per array and forward, shared
+        # by the groups as the sequences of one reference call share it
+        layers = list(self.layers)
+        uses = len(hs)
+        self._draw_noise(layers[0], uses, False)     # nothing runs yet for a background pass to overlap
+        for i, layer in enumerate(layers):
+            if i + 1 < len(layers):
+                self._draw_noise(layers[i + 1], uses, self.prefetch_noise)
+            elif self.prefetch_noise:
+                self._draw_noise(self.lm_head, 1, True)
             for m in range(len(hs)):
                 settle(m)
                 launch(m, layer.attn_partial(hs[m], cos, sin))

@@ -79,3 +79,31 @@ def test_noise_statistics(mode, cuda):
     spread = np.hypot(mine[:, 2].std(ddof=1), ref_mean.std(ddof=1)) / np.sqrt(SEEDS)
     print(f"{mode}: err mean vs exact mine {mine[:, 2].mean():.4f} ref {ref_mean.mean():.4f} +- {spread:.4f}")
     assert abs(mine[:, 2].mean() - ref_mean.mean()) < max(0.02 * abs(ref_mean.mean()), 4 * spread)
+
+
+def test_shared_and_background_read_noise_draws(cuda):
+    """DPETensor.draw_read_noise: a draw taken for two multiplies serves both (bit-identical outputs, as
+    the sequences of one reference call share one draw); a third multiply draws again; the background
+    pass (side stream, one small block per SM) produces the same planes as the foreground one for the
+    same seed; and a draw taken in the background beside a running multiply is waited for."""
+    import memintelli_flash_b200 as M
+    eng = M.DPETensor(device=cuda, HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.0,
+                      rate_stuck_HGS=0.0, rate_stuck_LGS=0.0, read_variation=0.05, vnoise=0.0)
+    g = torch.Generator().manual_seed(3)
+    x, w = torch.randn(512, 1024, generator=g), torch.randn(1024, 768, generator=g) * 0.03
+    sm = torch.tensor([1, 1, 2, 2, 2])
+    xs = M.SlicedData(sm, is_weight=False, paral_size=(1, 32), quant_gran=(1, 128), device=cuda, inference=True)
+    ws = M.SlicedData(sm, is_weight=True, paral_size=(32, 32), quant_gran=(128, 128), device=cuda, inference=True)
+    xs.slice_data_imp(eng, x.to(cuda))
+    ws.slice_data_imp(eng, w.to(cuda))
+    outs = {}
+    for background in (False, True):
+        torch.manual_seed(21)
+        big = eng(xs, ws)                       # queued work for a background pass to run beside
+        eng.draw_read_noise(ws, uses=2, background=background)
+        a, b = eng(xs, ws), eng(xs, ws)
+        c = eng(xs, ws)                         # the shared draw is used up: a new one
+        torch.cuda.synchronize()
+        assert torch.equal(a, b) and not torch.equal(a, c) and not torch.equal(a, big)
+        outs[background] = a
+    assert torch.equal(outs[False], outs[True])

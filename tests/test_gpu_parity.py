@@ -84,20 +84,29 @@ def test_tile_sums_bit_exact(name, cuda):
 
 
 def test_write_variation_deterministic(cuda):
-    """Write variation (fixed seed 42) without read noise: deterministic and statistically equivalent.
+    """Write variation (fixed seed 42) without read noise: deterministic, and as close to the reference
+    as a float evaluation can be.
 
-    Non-integer conductances enter the tensor cores as FP16 (11-bit significand),
-    so a few ADC codes next to rounding boundaries differ from the reference's
-    fp32 evaluation; the effect on the output is far below the write variation's.
-    """
+    The non-integer conductances enter the tensor cores as FP16 hi and lo planes (22 significand bits)
+    accumulated in fp32.  A crossbar sum next to an ADC rounding boundary can still round the other way
+    than in the reference's fp32 evaluation: the oracle's own fp32 and fp64 evaluations differ from the
+    reference by 1.2e-4 and 2.3e-4 (norm).  The result must stay within 2x the fp64 oracle's distance
+    of the reference, and match the fp64 oracle as closely."""
     c = G.case("write_var")
     eng, xs, ws = gpu_pair(c, cuda)
     y = eng(xs, ws).cpu().numpy().astype(np.float64)
     y_ref = c["golden"]["y"].astype(np.float64)
-    assert rel_norm(y, y_ref) < 1e-2
+    oxs, ows, oeng, _ = oracle_pair(c)
+    y64 = O.mvm_float(oxs, ows, oeng, np.random.default_rng(0), c["fields"].get("stuck"), c["fields"]["write"],
+                      noisy=False)
+    d_ref, d_orc = rel_norm(y, y_ref), rel_norm(y, y64)
+    print(f"write variation: vs reference {d_ref:.3e}, vs fp64 oracle {d_orc:.3e}, "
+          f"oracle vs reference {rel_norm(y64, y_ref):.3e}")
+    assert d_ref < 2 * rel_norm(y64, y_ref)
+    assert d_orc < 2 * rel_norm(y64, y_ref)
     ideal = c["x"].astype(np.float64) @ c["w"].astype(np.float64)
     snr = lambda a: 10 * np.log10(np.sum(ideal ** 2) / np.sum((ideal - a) ** 2))
-    assert abs(snr(y) - snr(y_ref)) < 0.1
+    assert abs(snr(y) - snr(y_ref)) < 0.01
     y2 = eng(xs, ws).cpu().numpy().astype(np.float64)
     assert np.array_equal(y, y2)
 

@@ -52,8 +52,14 @@ def _worker(rank, world, port, q):
             dist.all_reduce(z)
             ref = ref + z
         for groups in (2, 3):
-            fake = SimpleNamespace(micro_batches=groups, layers=layers, group=None)
+            draws = []                 # (array owner, uses, background) of every read-noise draw
+            fake = SimpleNamespace(micro_batches=groups, layers=layers, group=None, prefetch_noise=True,
+                                   lm_head="lm_head", _draw_noise=lambda what, uses, bg: draws.append((what, uses, bg)))
             got = Qwen3CimPrefill._layers_overlapped(fake, h0.clone(), None, None)
+            # one draw per layer shared by the groups: layer 0 up front, each next layer (then lm_head, used
+            # once) in the background of the layer before it
+            assert draws == [(layers[0], groups, False)] + [(l, groups, True) for l in layers[1:]] + \
+                [("lm_head", 1, True)]
             q.put((rank, groups, float((got - ref).abs().max())))
     finally:
         dist.destroy_process_group()
