@@ -269,10 +269,15 @@ def dp_tp_layout(world, rank, batch, tp=0):
 # half of a packed f32x2 rounding FMA, of which the FMA-heavy pipe takes half: 1.5 FMA-heavy lane operations
 # per event at 64 lanes per clock per SM (16 per sub-partition) caps it at 42.7 events per SM clock.
 MVM_FMAHEAVY_OPS_PER_ADC_EVENT = 1.5
-# DRAM bytes per ADC event of the fused MVM (dram__bytes_read.sum + dram__bytes_write.sum of one launch
-# divided by its ADC events), from the capture in profiles/mvm_kernel_4096.md; the bench scales it by the
-# ADC events of its launches.
-MVM_DRAM_BYTES_PER_ADC_EVENT = (1.48e9 + 68e6) / 5.369e10
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of each crossbar array of the
+# one-GPU forward, captured with ncu at the bench's shapes and device model (profiles/mvm_dram_qwen3_shapes.md);
+# lm_head counts as four launches of a quarter of its columns.  Averaged over the forward's 113 launches this
+# is the roofline's per-launch traffic at N = 1 (other layouts run other shapes: reported as null there).
+MVM_DRAM_BYTES_LAYER = {"qkv": 242.7e6 + 253.1e6, "o": 359.8e6 + 59.7e6, "gate_up": 673.8e6 + 379.0e6,
+                        "down": 670.8e6 + 65.5e6}
+MVM_DRAM_BYTES_LM_HEAD = 4 * (3448.9e6 + 2479.6e6)
+MVM_DRAM_BYTES_PER_LAUNCH_1GPU = ((ARCH["layers"] * sum(MVM_DRAM_BYTES_LAYER.values()) + MVM_DRAM_BYTES_LM_HEAD)
+                                  / (4 * ARCH["layers"] + 1))
 
 
 class Layout:
@@ -438,7 +443,10 @@ def run_b200(args):
                 "sliced_mvm_tops": ops_per_token() * tokens / (ms / 1000.0) / 1e12,
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak,
-                             "traffic": MVM_DRAM_BYTES_PER_ADC_EVENT * r["mvm_adc"] / max(r["launches"], 1),
+                             "traffic": MVM_DRAM_BYTES_PER_LAUNCH_1GPU if world == 1 else None,
+                             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum per launch of each "
+                                               "array shape, averaged over one forward's launches"
+                                               if world == 1 else "not captured for this layout's shapes",
                              "peak_kind": f"bf16 sustained ({peak_kind})",
                              "kernel": "mvm_kernel (fused crossbar MVM)", "launches": r["launches"],
                              "kernel_share": mvm_ms / ms if ms else None,

@@ -96,6 +96,11 @@ struct MvmArgs {
   // tail_splits K ranges of tail_tiles_per_split K tiles; CTA b takes range b % tail_splits of tile
   // dp_tiles + b / tail_splits and writes it to tail_partial[b][128][BN], summed by tail_reduce.
   int64_t dp_tiles;
+  // Tile order of a persistent launch: bands of tile_band_rows row tiles, each band column by column.
+  // 1 (row by row) keeps each row tile's input planes in L2 while all weight columns pass; a weight
+  // operand too large for L2 (a wide lm_head) gets bands whose input planes fit, so that the weights
+  // stream from DRAM once per band instead of once per row tile.
+  int64_t tile_band_rows;
   int32_t tail_splits;
   int32_t tail_tiles_per_split;
   float* tail_partial;
@@ -132,7 +137,7 @@ cudaError_t launch_splitk_reduce(const float* partial, int splits, int64_t M, in
                                  int64_t col_stride, const float* bias, cudaStream_t stream);
 int mvm_column_groups(int sy);   // output tile width BN = 16 * mvm_column_groups(Sy)
 cudaError_t launch_tail_reduce(const float* tail_partial, int splits, int64_t dp_tiles, int64_t tail_tiles, int bn,
-                               int64_t M, int64_t N, float* y, int64_t rows_per_group, int64_t group_stride,
+                               int64_t band, int64_t M, int64_t N, float* y, int64_t rows_per_group, int64_t group_stride,
                                int64_t row_stride, int64_t col_stride, const float* bias, cudaStream_t stream);
 // Multiprocessor count of `device`, cached per device.
 cudaError_t device_sm_count(int device, int* sms);

@@ -846,6 +846,16 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
     if (t2.splits > 1 && workspace_floats >= t2.floats) tl = t2;
   }
   a.dp_tiles = tl.dp_tiles;
+  {
+    // a weight operand within 48 MB stays in L2 across row tiles; a larger one is streamed once per band
+    // of row tiles whose input planes (about 24 MB) stay in L2 instead
+    const double es = esize(kind);
+    const double b_bytes = static_cast<double>(n) * kg->kt * kg->pp * es * b_planes_n;
+    const double a_tile_bytes = static_cast<double>(mib::kMvmBM) * kg->kt * kg->pp * es * tx.S;
+    int64_t band = 1;
+    if (b_bytes > 48e6) band = std::max<int64_t>(1, std::min<int64_t>(16, static_cast<int64_t>(24e6 / a_tile_bytes)));
+    a.tile_band_rows = band;
+  }
   a.tail_splits = tl.splits;
   a.tail_tiles_per_split = tl.tiles_per_split;
   a.tail_partial = tl.splits > 1 ? workspace : nullptr;
@@ -867,7 +877,8 @@ int mib_mvm(const void* a_planes, const float* a_scale, int64_t m, const mib_sli
   }
   if (a.tail_partial) {
     const int64_t tiles = ((n + bn - 1) / bn) * ((m + mib::kMvmBM - 1) / mib::kMvmBM);
-    e = mib::launch_tail_reduce(a.tail_partial, tl.splits, tl.dp_tiles, tiles - tl.dp_tiles, bn, m, n, y,
+    e = mib::launch_tail_reduce(a.tail_partial, tl.splits, tl.dp_tiles, tiles - tl.dp_tiles, bn, a.tile_band_rows, m,
+                                n, y,
                                 a.rows_per_group, a.group_stride, a.row_stride, a.col_stride, bias, stream);
     if (e != cudaSuccess) return cuda_fail(e, "tail reduce launch");
   }

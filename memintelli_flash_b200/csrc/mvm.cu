@@ -35,17 +35,16 @@ constexpr int kSlotCols = 256;
 constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23: x + magic rounds x to an integer (half-even)
 constexpr uint32_t kMagicBits = 0x4B400000u;
 
-// Order in which a persistent launch steps through the output tiles: bands of kTileBandRows row tiles,
-// each band column by column (row tiles fastest).  The SMs then work on one band's rows at a time and
-// every weight column tile is read from DRAM once per band, not once per row tile: for a 1024 x 151936
-// lm_head at 16384 rows that is 8 passes over the weights instead of 128.
-constexpr int64_t kTileBandRows = 16;
-__host__ __device__ __forceinline__ void tile_coords(int64_t idx, int64_t n_tiles_m, int64_t n_tiles_n,
+// Order in which a persistent launch steps through the output tiles: bands of `band` row tiles, each
+// band column by column (row tiles fastest).  band = 1 is row by row.  With wider bands the SMs work on
+// one band's rows at a time and every weight column tile is read from DRAM once per band, not once per
+// row tile (MvmArgs::tile_band_rows says when the host widens them).
+__host__ __device__ __forceinline__ void tile_coords(int64_t idx, int64_t n_tiles_m, int64_t n_tiles_n, int64_t band,
                                                      int64_t* tm, int64_t* tn) {
-  const int64_t band = idx / (kTileBandRows * n_tiles_n);
-  const int64_t first = band * kTileBandRows;
-  const int64_t rows = n_tiles_m - first < kTileBandRows ? n_tiles_m - first : kTileBandRows;
-  const int64_t local = idx - band * kTileBandRows * n_tiles_n;
+  const int64_t b = idx / (band * n_tiles_n);
+  const int64_t first = b * band;
+  const int64_t rows = n_tiles_m - first < band ? n_tiles_m - first : band;
+  const int64_t local = idx - b * band * n_tiles_n;
   *tm = first + local % rows;
   *tn = local / rows;
 }
@@ -136,13 +135,13 @@ __global__ void __launch_bounds__(32 * (4 * column_groups(SY) + 2), 1)
   auto tile_m0 = [&](int64_t it) -> int64_t {
     if (!kPersist) return static_cast<int64_t>(blockIdx.y) * kMvmBM;
     int64_t tm, tn;
-    tile_coords(item_tile(it), n_tiles_m, n_tiles_n, &tm, &tn);
+    tile_coords(item_tile(it), n_tiles_m, n_tiles_n, P.tile_band_rows, &tm, &tn);
     return tm * kMvmBM;
   };
   auto tile_n0 = [&](int64_t it) -> int64_t {
     if (!kPersist) return static_cast<int64_t>(blockIdx.x) * BN;
     int64_t tm, tn;
-    tile_coords(item_tile(it), n_tiles_m, n_tiles_n, &tm, &tn);
+    tile_coords(item_tile(it), n_tiles_m, n_tiles_n, P.tile_band_rows, &tm, &tn);
     return tn * BN;
   };
   constexpr int Sy = SY;
@@ -527,7 +526,8 @@ cudaError_t launch_kind(const CUtensorMap& ta, const CUtensorMap& tb, const MvmA
 // Tail reduction of a persistent launch: every element of the tail tiles is the sum, in K order, of
 // its tail_splits partials (tail_partial[tile * splits + s][row][col], tile-local), plus the bias.
 __global__ void tail_reduce_kernel(const float* __restrict__ tail_partial, int splits, int64_t dp_tiles,
-                                   int64_t tail_tiles, int bn, int64_t M, int64_t N, float* __restrict__ y,
+                                   int64_t tail_tiles, int bn, int64_t band, int64_t M, int64_t N,
+                                   float* __restrict__ y,
                                    int64_t rows_per_group, int64_t group_stride, int64_t row_stride,
                                    int64_t col_stride, const float* __restrict__ bias) {
   const int64_t per_tile = static_cast<int64_t>(kMvmBM) * bn;
@@ -538,7 +538,7 @@ __global__ void tail_reduce_kernel(const float* __restrict__ tail_partial, int s
     const int64_t tl = e / per_tile, rem = e - tl * per_tile;
     const int64_t r = rem / bn, c = rem - r * bn;
     int64_t tm, tn;
-    tile_coords(dp_tiles + tl, n_tiles_m, n_tiles_n, &tm, &tn);
+    tile_coords(dp_tiles + tl, n_tiles_m, n_tiles_n, band, &tm, &tn);
     const int64_t m = tm * kMvmBM + r, n = tn * bn + c;
     if (m >= M || n >= N) continue;
     float v = 0.0f;
@@ -581,12 +581,12 @@ cudaError_t device_sm_count(int device, int* sms) {
 }
 
 cudaError_t launch_tail_reduce(const float* tail_partial, int splits, int64_t dp_tiles, int64_t tail_tiles, int bn,
-                               int64_t M, int64_t N, float* y, int64_t rows_per_group, int64_t group_stride,
+                               int64_t band, int64_t M, int64_t N, float* y, int64_t rows_per_group, int64_t group_stride,
                                int64_t row_stride, int64_t col_stride, const float* bias, cudaStream_t stream) {
   const int64_t total = tail_tiles * kMvmBM * bn;
   const int64_t blocks = (total + 255) / 256;
   tail_reduce_kernel<<<static_cast<unsigned>(blocks < 4096 ? blocks : 4096), 256, 0, stream>>>(
-      tail_partial, splits, dp_tiles, tail_tiles, bn, M, N, y, rows_per_group, group_stride, row_stride, col_stride,
+      tail_partial, splits, dp_tiles, tail_tiles, bn, band, M, N, y, rows_per_group, group_stride, row_stride, col_stride,
       bias);
   count_launch();
   return cudaGetLastError();
