@@ -219,3 +219,43 @@ def test_engine_on_second_device_while_first_is_current():
     ref = O.mvm_exact(oxs, ows, oeng, wl)
     assert rel_norm(y1.double().cpu().numpy(), ref) <= 1e-5
     assert torch.equal(y0.cpu(), y1.cpu())
+
+
+def test_write_variation_split_weights_at_a_tail_split_shape(cuda):
+    """The FP16 hi/lo weight operand (write variation 0.05) through the persistent launch with several
+    tiles per CTA, three pipeline stages (the doubled weight stage) and a tail split: 2048 x 1024 x 4096
+    is 1376 output tiles, 9 waves + 44 tiles cut into K ranges.  128 rows against the oracle's fp64
+    evaluation with the same fixed-seed write field (torch.normal, Generator(42), the reference's G shape),
+    within the distance the small golden case shows between float evaluations (2.3e-4)."""
+    import memintelli_flash_b200 as M
+    from memintelli_flash_b200 import _native as N
+    M_, K, Nc = 2048, 1024, 4096
+    kw = dict(HGS=1e-5, LGS=1e-8, rdac=4, g_level=4, radc=4096, write_variation=0.05, read_variation=0.0,
+              vnoise=0.0, rate_stuck_HGS=0.0, rate_stuck_LGS=0.0)
+    eng = M.DPETensor(device=cuda, **kw)
+    eng.fault_field_device = "cpu"
+    g = torch.Generator().manual_seed(8)
+    x, w = torch.randn(M_, K, generator=g), torch.randn(K, Nc, generator=g) * 0.03
+    sm = [1, 1, 2, 2, 2]
+    xs = M.SlicedData(torch.tensor(sm), is_weight=False, paral_size=(1, 32), quant_gran=(1, 128), device=cuda,
+                      inference=True)
+    ws = M.SlicedData(torch.tensor(sm), is_weight=True, paral_size=(32, 32), quant_gran=(128, 128), device=cuda,
+                      inference=True)
+    ws.slice_data_imp(eng, w.to(cuda))
+    xs.slice_data_imp(eng, x.to(cuda))
+    f = N.c_i64(0)
+    N.call("mib_mvm_workspace", M_, Nc, xs._spec(), ws._spec(), xs._kgeom(), eng._device_spec(), f)
+    assert 0 < f.value < 2 * M_ * Nc                     # the tail split's partials
+    y = eng(xs, ws)
+    torch.cuda.synchronize()
+    rows = np.arange(0, M_, 16) + (np.arange(128) * 5) % 16
+    oxs = O.slice_matrix(x[rows].numpy(), sm, None, (1, 32), (1, 128))
+    ows = O.slice_matrix(w.numpy(), sm, None, (32, 32), (128, 128))
+    gshape = (ows.geom.rows_p // 32, ows.geom.cols_p // 32, len(sm), 32, 32)
+    write = torch.normal(0, 0.05, gshape, generator=torch.Generator().manual_seed(42)).numpy()
+    ref = O.mvm_float(oxs, ows, O.Engine(**kw), np.random.default_rng(0), None, write, noisy=False)
+    got = y[torch.from_numpy(rows).to(cuda)].double().cpu().numpy()
+    d = rel_norm(got, ref)
+    print(f"write variation 2048x1024x4096: vs fp64 oracle {d:.3e}")
+    assert d < 5e-4
+    N.device_status()
